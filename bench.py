@@ -1,0 +1,350 @@
+"""Benchmark of the B200 VC-attention path (driver contract: one JSON line).
+
+Workload (default): non-causal BNSD [1,28,37741,128] bf16,
+Q,K ~ N(0,1) with a K channel mean ~ N(0,3), V ~ N(0,1), ExpCast on,
+smoothing off; synthetic, seeded per (b,h) head so shards are slices of the
+single-GPU tensors.  A step is one full ``sageattn_vc`` call: INT8 Q/K + FP8 V
+preparation and the fused attention kernel, inputs resident in HBM (the
+811 MB of inputs exceed the 126 MB L2, so no flush is needed).
+
+  value  = 4*B*H*S^2*D / t_step  (TOPS, all ranks, max-over-ranks device time)
+  e2e    = same metric through the public API with pinned host buffers:
+           H2D of the inputs + the call + D2H of the output every step
+  roofline: the fused attention kernel, CUDA-event timed inside the region
+  cpu_baseline: the CPU oracle (a restatement of the reference's own CPU
+           path) on a bounded sample, extrapolated linearly
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c2]
+Multi-GPU: torchrun --nproc-per-node N bench.py --gpus N (units split across
+ranks; no collective in the timed region).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "cake-opt-vc_attention_b200"))
+sys.path.insert(0, str(REPO))
+
+import torch  # noqa: E402
+
+CONFIGS = {
+    # name: B, H, S, D, dtype, k_mean_std, v_smooth, description
+    "c2": (1, 28, 37741, 128, torch.bfloat16, 3 ** 0.5, False,
+           "BNSD [1,28,37741,128] bf16, ExpCast on, smoothing off"),
+    "c3": (1, 28, 37741, 128, torch.bfloat16, 3 ** 0.5, True,
+           "BNSD [1,28,37741,128] bf16, ExpCast + V grouping + 128-token block smoothing"),
+    "c4": (2, 24, 16384, 64, torch.bfloat16, 3 ** 0.5, False, "BNSD [2,24,16384,64] bf16 D64, ExpCast on"),
+    "c5": (2, 40, 75600, 128, torch.bfloat16, 3 ** 0.5, True,
+           "BNSD [2,40,75600,128] bf16, ExpCast + V block smoothing"),
+}
+METRIC = "TOPS (4*B*H*S^2*D per call) at BNSD [1,28,37741,128] D128, sageattn_vc ExpCast (prep + fused kernel)"
+
+
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def gen_head(bh: int, S: int, D: int, dtype, k_std: float, smooth: bool, device, seed: int = 0):
+    """Seeded synthetic Q,K,V for one flattened (b,h) head."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed * 1000003 + bh)
+    q = torch.randn(S, D, generator=g, device=device)
+    k = torch.randn(S, D, generator=g, device=device) + torch.randn(D, generator=g, device=device) * k_std
+    if smooth:
+        cent = torch.randn(16, D, generator=g, device=device) * 2 ** 0.5
+        lab = torch.randint(0, 16, (S,), generator=g, device=device)
+        v = cent[lab] + 0.3 * torch.randn(S, D, generator=g, device=device)
+    else:
+        v = torch.randn(S, D, generator=g, device=device)
+    return q.to(dtype), k.to(dtype), v.to(dtype)
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline_sample(B, H, S, D, dtype, k_std, smooth, threads=None):
+    """Time the CPU oracle on one head's preparation plus 128 query rows
+    against all keys; extrapolate linearly to the full workload."""
+    from oracle import vc_oracle as O
+    if threads:
+        torch.set_num_threads(threads)
+    q, k, v = gen_head(0, S, D, dtype, k_std, smooth, "cpu")
+    q, k, v = (x.reshape(1, 1, S, D) for x in (q, k, v))
+    t0 = time.perf_counter()
+    st = O.prepare(q, k, v, expcast=True, v_smooth=smooth, km=O.k_mean(k))
+    t_prep = time.perf_counter() - t0
+    rows = torch.arange(0, S, max(1, S // 128))[:128]
+    t0 = time.perf_counter()
+    O.reference(st, query_indices=rows, chunk=128)
+    t_ref = time.perf_counter() - t0
+    t_full = B * H * (t_prep + t_ref * (S / rows.numel()))
+    ops_full = 4.0 * B * H * S * S * D
+    return {"value": ops_full / t_full / 1e12, "unit": "TOPS", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"CPU oracle: head-0 prep ({t_prep:.2f}s) + {rows.numel()} query rows x {S} keys "
+                      f"({t_ref:.2f}s), extrapolated linearly to {B*H} heads x {S} rows",
+            "seconds_extrapolated": t_full}
+
+
+def run_reference(args, cfg):
+    """--impl reference: the CPU oracle of the reference's path on host cores."""
+    B, H, S, D, dtype, k_std, smooth, desc = cfg
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline_sample(B, H, S, D, dtype, k_std, smooth, threads)
+        if i >= args.warmup:
+            vals.append(r)
+    value = statistics.median(v["value"] for v in vals)
+    ms = 4.0 * B * H * S * S * D / (value * 1e12) * 1e3
+    line = {"metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8/e4m3 (decoded FP32 CPU emulation)", "data": "synthetic",
+            "config": {"workload": desc, "impl": "reference"}, "impl": "reference",
+            "cpu_baseline": {**vals[-1], "value": value},
+            "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--config", choices=tuple(CONFIGS), default="c2")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gather", action="store_true", help="also time the optional NCCL all-gather of outputs")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference(args, cfg)
+        return
+    B, H, S, D, dtype, k_std, smooth, desc = cfg
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    from vc_b200 import ops, parallel
+    from vc_b200 import _native
+    _native.load()
+    sh = parallel.shard(B, H, S, world, rank)
+    nbh = sh.bh_end - sh.bh_begin
+    # this rank's heads, generated on the device
+    qh, kh, vh = [], [], []
+    for bh in range(sh.bh_begin, sh.bh_end):
+        a, b_, c = gen_head(bh, S, D, dtype, k_std, smooth, dev)
+        qh.append(a), kh.append(b_), vh.append(c)
+    q = torch.stack(qh).reshape(1, nbh, S, D)
+    k = torch.stack(kh).reshape(1, nbh, S, D)
+    v = torch.stack(vh).reshape(1, nbh, S, D)
+    del qh, kh, vh
+    # a Shard relative to the local head block
+    local_shard = parallel.Shard(0, 1, sh.unit_begin - sh.bh_begin * sh.qtiles,
+                                 sh.unit_end - sh.bh_begin * sh.qtiles, 0, nbh, sh.qtiles)
+    from sageattention_local.vc import prepare
+    out = torch.empty((1, nbh, S, D), dtype=dtype, device=dev)
+    mean_numel = (B * H * D, B * H * S * D)
+    att_events = []
+
+    def step(record=False):
+        st = prepare(q, k, v, expcast=True, v_smooth=smooth, mean_numel=mean_numel)
+        if record:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+        ops.attention_fwd(st["q"], st["qs"], st["k"], st["ks"], st["v"], st["vs"], st["means"], out=out,
+                          sm_scale=st["scale"], expcast=True, block_values=smooth,
+                          unit_range=local_shard.local_units)
+        if record:
+            e1.record()
+            att_events.append((e0, e1))
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    with clocks:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        t0.record()
+        for _ in range(args.steps):
+            step(record=True)
+        t1.record()
+        torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / args.steps
+    att_ms = statistics.mean(a.elapsed_time(b) for a, b in att_events)
+    if dist:
+        tt = torch.tensor([ms, att_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms, att_ms = tt.tolist()
+    ops_total = 4.0 * B * H * S * S * D
+    value = ops_total / (ms * 1e-3) / 1e12
+    err = ops.error_word(local, clear=True)
+    if err:
+        raise RuntimeError(f"device error word {err:#x} after the timed region")
+
+    # roofline of the fused attention kernel (this rank's launch)
+    rows_local = sum(min(128, S - (u % sh.qtiles) * 128) for u in range(sh.unit_begin, sh.unit_end))
+    ops_launch = 4.0 * rows_local * S * D
+    hbm, bf16, bf16_sus, basis = peaks()
+    peak_tops = 2.0 * bf16          # dense INT8/FP8 tensor rate is 2x the measured dense BF16 rate
+    achieved = ops_launch / (att_ms * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_tops, "unit": "TFLOP/s",
+                "frac": achieved / peak_tops, "traffic": None,
+                "kernel": "vc_attention_kernel", "peak_basis": f"2 x bf16_tflops ({basis}, MEASURED_PEAKS.json)",
+                "kernel_ms": att_ms}
+
+    # end to end through the public API with pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+        hout = torch.empty((1, nbh, S, D), dtype=dtype).pin_memory()
+
+        def e2e_step():
+            dq, dk, dv = (x.to(dev, non_blocking=True) for x in (hq, hk, hv))
+            if world == 1:
+                from sageattention_local import sageattn_vc
+                o = sageattn_vc(dq, dk, dv, v_smooth=smooth)
+            else:
+                o = parallel.sharded_attention(dq, dk, dv, local_shard, v_smooth=smooth)
+            hout.copy_(o, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        n_e2e = max(3, min(args.steps, 5))
+        for _ in range(n_e2e):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / n_e2e
+        if dist:
+            tt = torch.tensor([e2e_ms], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            e2e_ms = tt.item()
+        e2e = {"value": ops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS", "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": 3 * nbh * S * D * q.element_size(),
+               "d2h_bytes_per_step": nbh * S * D * q.element_size(),
+               "path": "sageattn_vc(q,k,v) on pinned-host inputs (per-rank shard for N>1)"}
+
+    gather_ms = None
+    if args.gather and dist:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        parallel.gather_rows(out, sh, B, H, S)
+        e1.record()
+        torch.cuda.synchronize()
+        gather_ms = e0.elapsed_time(e1)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_sample(B, H, S, D, dtype, k_std, smooth)
+
+    if rank == 0:
+        launches_per_step = 4 + 2 + 1 + (0 if not smooth else 6)
+        line = {"metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "int8 QK / e4m3 PV (fp32 accumulate), bf16 I/O",
+                "data": "synthetic (seeded per head on device)",
+                "config": {"workload": desc, "B": B, "H": H, "S": S, "D": D, "expcast": True, "v_smooth": smooth,
+                           "parallelism": f"units split over {world} rank(s), outputs sharded",
+                           "l2": "inputs (811 MB) exceed the 126 MB L2; no flush needed"},
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
+                "gpu_launches": launches_per_step * args.steps, "attention_ms": att_ms}
+        if gather_ms is not None:
+            line["allgather_ms"] = gather_ms
+        print(json.dumps(line))
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

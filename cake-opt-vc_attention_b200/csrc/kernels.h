@@ -1,0 +1,85 @@
+// Internal launcher interfaces between the C ABI (capi.cu) and the kernels.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+#include "vc_b200.h"
+
+namespace vcb {
+
+struct PrepQKArgs {
+  const void* q;
+  const void* k;
+  int dtype;
+  int64_t B, H, Sq, Sk, D;
+  int64_t qsb, qsh, qss, ksb, ksh, kss;
+  const int64_t* perm;
+  const void* km_in;
+  void* km_out;
+  int64_t mean_numel_out, mean_numel_in;
+  int8_t* q8;
+  float* qs;
+  int8_t* k8;
+  float* ks;
+  void* workspace;
+};
+int64_t prep_qk_workspace(int64_t B, int64_t H, int64_t Sk, int64_t D);
+int prep_qk(const PrepQKArgs& a, cudaStream_t st);
+
+struct PrepVArgs {
+  const void* v;
+  int dtype;
+  int64_t B, H, S, D;
+  int64_t sb, sh, ss;
+  const int64_t* perm;
+  int channel_scale;  // blocks mode only
+  int demean;         // blocks mode only
+  uint8_t* v8;
+  float* vs;
+  uint16_t* means;    // blocks mode only
+  void* workspace;
+};
+int64_t prep_v_channel_workspace(int64_t B, int64_t H, int64_t S, int64_t D);
+int prep_v_channel(const PrepVArgs& a, cudaStream_t st);
+int64_t prep_v_blocks_workspace(int64_t B, int64_t H, int64_t S, int64_t D);
+int prep_v_blocks(const PrepVArgs& a, cudaStream_t st);
+
+struct GroupArgs {
+  const void* v;
+  int dtype;
+  int64_t B, H, S, D;
+  int64_t sb, sh, ss;
+  int clusters, iterations;
+  const float* centers_in;
+  int64_t* perm_out;
+  int32_t* labels_out;
+  float* centers_out;
+  void* workspace;
+};
+int64_t group_values_workspace(int64_t B, int64_t H, int64_t S, int64_t D, int clusters);
+int group_values(const GroupArgs& a, cudaStream_t st);
+
+struct AttnArgs {
+  const int8_t* q8;
+  const float* qs;
+  const int8_t* k8;
+  const float* ks;
+  const uint8_t* v8;
+  const float* vs;
+  const uint16_t* means;
+  void* out;
+  int out_dtype;
+  int64_t B, H, Sq, Sk, D;
+  int64_t osb, osh, oss;
+  int expcast, block_values, vs_per_block;
+  float sm_scale;
+  int64_t unit_begin, unit_end;
+};
+int attention_fwd(const AttnArgs& a, cudaStream_t st);
+int attention_resources(int head_dim, int64_t* out4);
+
+int expcast_codes(const float* x, uint8_t* y, int64_t n, cudaStream_t st);
+
+// Host-side error text for the calling thread.
+void set_last_error(const char* fmt, ...);
+
+}  // namespace vcb

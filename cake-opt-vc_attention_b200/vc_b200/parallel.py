@@ -1,0 +1,114 @@
+"""Multi-GPU partitioning of the VC-attention path.
+
+Work units are (b*H + h, q_tile) pairs flattened as ``(b*H+h)*ceil(Sq/128) +
+q_tile``.  Every unit is independent given its head's full K/V payloads, so a
+rank owns a contiguous unit range, prepares only the heads that range
+touches (at most one extra head of redundant K/V preparation per boundary)
+and computes its output rows locally.  Outputs stay sharded; an optional
+NCCL all-gather assembles the full tensor.  No data-path collective.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+
+@dataclass(frozen=True)
+class Shard:
+    rank: int
+    world: int
+    unit_begin: int      # global unit range [unit_begin, unit_end)
+    unit_end: int
+    bh_begin: int        # flattened (b*H+h) heads touched [bh_begin, bh_end)
+    bh_end: int
+    qtiles: int
+
+    @property
+    def local_units(self) -> tuple[int, int]:
+        """Unit range relative to the first touched head."""
+        off = self.bh_begin * self.qtiles
+        return self.unit_begin - off, self.unit_end - off
+
+    @property
+    def num_units(self) -> int:
+        return self.unit_end - self.unit_begin
+
+
+def shard(B: int, H: int, Sq: int, world: int, rank: int) -> Shard:
+    """Balanced contiguous split of the unit space (sizes differ by <= 1)."""
+    if not 0 <= rank < world:
+        raise ValueError("rank out of range")
+    qtiles = (Sq + 127) // 128
+    total = B * H * qtiles
+    base, extra = divmod(total, world)
+    ub = rank * base + min(rank, extra)
+    ue = ub + base + (1 if rank < extra else 0)
+    if ue > ub:
+        bh0, bh1 = ub // qtiles, (ue - 1) // qtiles + 1
+    else:
+        bh0 = bh1 = min(ub // qtiles, B * H)
+    return Shard(rank, world, ub, ue, bh0, bh1, qtiles)
+
+
+def head_slice(x: torch.Tensor, s: Shard) -> torch.Tensor:
+    """[B,H,S,D] -> [1, bh_end-bh_begin, S, D] view of the touched heads."""
+    B, H = x.shape[:2]
+    return x.reshape(1, B * H, *x.shape[2:])[:, s.bh_begin:s.bh_end]
+
+
+def sharded_attention(q, k, v, s: Shard, *, expcast=True, v_smooth=False, clusters=8, iterations=2,
+                      v_scale_mode="channel", sm_scale=None, out=None):
+    """Prepare the shard's heads and compute its units (HND inputs).
+
+    Returns the local output [1, nbh, Sq, D]; rows outside the shard's unit
+    range are not written.
+    """
+    from sageattention_local.vc import prepare
+    from . import ops
+    qh, kh, vh = head_slice(q, s), head_slice(k, s), head_slice(v, s)
+    # torch's CUDA mean factor over the full tensor, so shards match 1-GPU km
+    mean_numel = (k.shape[0] * k.shape[1] * k.shape[3], k.numel())
+    st = prepare(qh, kh, vh, expcast=expcast, v_smooth=v_smooth, clusters=clusters, iterations=iterations,
+                 sm_scale=sm_scale, v_scale_mode=v_scale_mode, mean_numel=mean_numel)
+    out_dtype = torch.float16 if q.dtype == torch.float16 else torch.bfloat16
+    return ops.attention_fwd(st["q"], st["qs"], st["k"], st["ks"], st["v"], st["vs"], st["means"],
+                             out_dtype=out_dtype, sm_scale=st["scale"], expcast=expcast, block_values=v_smooth,
+                             out=out, unit_range=s.local_units)
+
+
+def gather_rows(local: torch.Tensor, s: Shard, B: int, H: int, Sq: int, group=None) -> torch.Tensor:
+    """Assemble the full [B,H,Sq,D] output from every rank's shard with one
+    ``all_gather_into_tensor`` of fixed-size row blocks (NCCL over NVLink on
+    GPUs; gloo on CPU in tests)."""
+    import torch.distributed as dist
+    world = s.world
+    D = local.shape[-1]
+    rows_per_unit = 128
+    # pack this rank's unit rows into a fixed-size buffer (max units per rank)
+    max_units = -(-B * H * s.qtiles // world)
+    buf = torch.zeros(max_units * rows_per_unit, D, dtype=local.dtype, device=local.device)
+    lb, le = s.local_units
+    flat = local.reshape(-1, D)                       # [nbh * Sq, D]
+    for i, u in enumerate(range(lb, le)):
+        bh, qt = divmod(u, s.qtiles)
+        r0 = qt * 128
+        r1 = min(Sq, r0 + 128)
+        buf[i * 128:i * 128 + (r1 - r0)] = flat[bh * Sq + r0: bh * Sq + r1]
+    allbuf = torch.empty(world * buf.shape[0], D, dtype=local.dtype, device=local.device)
+    if hasattr(dist, "all_gather_into_tensor") and local.device.type == "cuda":
+        dist.all_gather_into_tensor(allbuf, buf, group=group)
+    else:
+        parts = list(allbuf.chunk(world))
+        dist.all_gather(parts, buf, group=group)
+        allbuf = torch.cat(parts)
+    out = torch.empty(B * H * Sq, D, dtype=local.dtype, device=local.device)
+    for r in range(world):
+        sr = shard(B, H, Sq, world, r)
+        blk = allbuf[r * buf.shape[0]:(r + 1) * buf.shape[0]]
+        for i, u in enumerate(range(sr.unit_begin, sr.unit_end)):
+            bh, qt = divmod(u, sr.qtiles)
+            r0 = qt * 128
+            r1 = min(Sq, r0 + 128)
+            out[bh * Sq + r0: bh * Sq + r1] = blk[i * 128:i * 128 + (r1 - r0)]
+    return out.reshape(B, H, Sq, D)

@@ -1,0 +1,288 @@
+"""GPU parity: the CUDA path (through the C ABI) against the CPU oracle.
+
+Bit-exact for INT8/E4M3/FP16 payloads and scales; attention outputs within
+cos >= 0.9999 and rel-L2 <= 1e-3 of the decoded-payload oracle (the
+tolerance stated by the reference's north star), also reported against FP32
+dense softmax attention.
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import vc_oracle as O
+from inputs import qk_inputs, mixture_values
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+COS_MIN, REL_MAX = 0.9999, 1e-3
+
+
+@pytest.fixture(scope="module")
+def ops(cuda_device):
+    from vc_b200 import ops as _ops
+    from vc_b200 import _native
+    _native.load()
+    _ops.error_word(0, clear=True)
+    yield _ops
+    torch.cuda.synchronize()
+    assert _ops.error_word(0, clear=True) == 0, "device error word set (a bounded wait timed out)"
+
+
+def _np(t):
+    return t.detach().cpu().numpy()
+
+
+def test_expcast_codes_bit_exact(ops):
+    f = np.load(GOLDEN / "expcast.npz")
+    x = torch.from_numpy(f["shifted"]).cuda()
+    assert np.array_equal(_np(ops.expcast_codes(x)), f["codes"])
+
+
+@pytest.mark.parametrize("name", ["c1_fp32", "tail_bf16_d64", "tail_fp16_d128", "single_bf16", "outlier_bf16"])
+def test_qk_int8_bit_exact_vs_reference_triton(ops, name):
+    f = np.load(GOLDEN / f"qk_{name}.npz")
+    dtype = getattr(torch, str(f["dtype"]))
+    q, k, _ = qk_inputs(int(f["seed"]), tuple(f["shape"]), dtype, float(f["koff"]), float(f["outliers"]))
+    km = torch.from_numpy(f["km"]).to(dtype).cuda()
+    q8, qs, k8, ks, _ = ops.prep_qk_int8(q.cuda(), k.cuda(), km=km)
+    torch.cuda.synchronize()
+    assert np.array_equal(_np(q8), f["q8"])
+    assert np.array_equal(_np(qs), f["qs"])
+    assert np.array_equal(_np(k8), f["k8"])
+    assert np.array_equal(_np(ks), f["ks"])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("shape", [(1, 2, 1000, 128), (2, 3, 257, 64), (1, 1, 5000, 128)])
+def test_k_mean_matches_torch_cuda_mean(ops, dtype, shape):
+    q, k, _ = qk_inputs(11, shape, dtype, 3 ** 0.5)
+    kc = k.cuda()
+    ref = kc.mean(dim=2, keepdim=True)
+    _, _, _, _, km = ops.prep_qk_int8(q.cuda(), kc, mean_numel=(shape[0] * shape[1] * shape[3], kc.numel()))
+    # FP32 summation order differs from torch's.  For half/bfloat16 the
+    # rounding to the input dtype hides it except for a tiny fraction of
+    # channels (one ulp); FP32 means differ only in their last bits.
+    if dtype != torch.float32:
+        diff = (km.float() != ref.float()).float().mean().item()
+        assert diff <= 0.02, diff
+    torch.testing.assert_close(km.float(), ref.float(), rtol=1e-2 if dtype != torch.float32 else 1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_qk_int8_with_device_mean_and_permutation(ops, dtype):
+    shape = (1, 2, 700, 128)
+    q, k, _ = qk_inputs(12, shape, dtype, 3 ** 0.5)
+    g = torch.Generator().manual_seed(3)
+    perm = torch.stack([torch.randperm(700, generator=g) for _ in range(2)]).reshape(1, 2, 700)
+    q8, qs, k8, ks, km = ops.prep_qk_int8(q.cuda(), k.cuda(), perm=perm.cuda())
+    kp = k.gather(2, perm.unsqueeze(-1).expand_as(k))
+    e_q8, e_qs, e_k8, e_ks = O.per_thread_int8(q, kp, km.cpu())
+    assert np.array_equal(_np(q8), e_q8) and np.array_equal(_np(qs), e_qs)
+    assert np.array_equal(_np(k8), e_k8) and np.array_equal(_np(ks), e_ks)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("dim", [64, 128])
+@pytest.mark.parametrize("n", [1, 127, 128, 129, 1000])
+def test_v_channel_bit_exact(ops, dtype, dim, n):
+    g = torch.Generator().manual_seed(n + dim)
+    v = (torch.randn(2, 2, n, dim, generator=g) * 3).to(dtype)
+    v[:, 1, :, 3] = 0                                       # all-zero channel -> zero-safe
+    v8, vs = ops.prep_v_channel(v.cuda())
+    e_v8, e_vs = O.v_channel_fp8(v.float().numpy())
+    assert np.array_equal(_np(vs), e_vs)
+    assert np.array_equal(_np(v8.view(torch.uint8)), e_v8)
+
+
+def _value_cases(dtype, dim, n):
+    g = torch.Generator().manual_seed(339)
+    v = torch.randn(2, 2, n, dim, generator=g)
+    for t, begin in enumerate(range(0, n, 128)):
+        v[:, :, begin:begin + 128] = v[:, :, begin:begin + 128] * (t + 1) + t * 3
+    v[..., 0] = 1.5
+    v[..., 1] = -2.0
+    return v.to(dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("dim", [64, 128])
+@pytest.mark.parametrize("n", [1, 127, 128, 129, 257])
+@pytest.mark.parametrize("channel", [False, True])
+def test_v_blocks_bit_exact(ops, dtype, dim, n, channel):
+    # the reference's 60-case preprocessing suite (scripts/validate_sage_vc.py:19-83)
+    v = _value_cases(dtype, dim, n)
+    v8, vs, means = ops.prep_v_blocks(v.cuda(), channel_scale=channel)
+    e_v8, e_vs, e_means = O.v_blocks_fp8(v.float().numpy(), channel_scale=channel)
+    assert np.array_equal(_np(vs), e_vs)
+    assert np.array_equal(_np(means).view(np.uint16), e_means.view(np.uint16))
+    assert np.array_equal(_np(v8.view(torch.uint8)), e_v8)
+
+
+def test_v_blocks_large_mean_overflow_guard(ops):
+    # reference tests/test_sage_vc_preprocess_cuda.py:48-65: near-constant
+    # blocks with huge means must keep mean/scale finite in FP16
+    v = torch.full((1, 1, 300, 64), 60000.0)
+    v[..., ::7, :] += 0.5
+    v8, vs, means = ops.prep_v_blocks(v.cuda(), channel_scale=True)
+    e_v8, e_vs, e_means = O.v_blocks_fp8(v.numpy(), channel_scale=True)
+    assert torch.isfinite(means.float()).all()
+    assert np.array_equal(_np(vs), e_vs) and np.array_equal(_np(v8.view(torch.uint8)), e_v8)
+
+
+def test_v_blocks_many_tiles_channel_reduction(ops):
+    # > 32 tiles exercise the channel reduction (reference test :68-80)
+    v = _value_cases(torch.bfloat16, 128, 128 * 40 + 3)
+    v8, vs, means = ops.prep_v_blocks(v.cuda(), channel_scale=True)
+    e_v8, e_vs, e_means = O.v_blocks_fp8(v.float().numpy(), channel_scale=True)
+    assert np.array_equal(_np(vs), e_vs)
+    assert np.array_equal(_np(v8.view(torch.uint8)), e_v8)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("dim", [64, 128])
+@pytest.mark.parametrize("n,count,iterations", [(1, 8, 2), (127, 3, 3), (129, 8, 2), (2049, 8, 2)])
+def test_group_values_matches_fp64_lloyd(ops, dtype, dim, n, count, iterations):
+    # well-separated clusters, as scripts/validate_sage_vc.py:86-117
+    g = torch.Generator().manual_seed(883)
+    c = min(n, count)
+    ids = torch.from_numpy(O.linspace_ids(n, c))
+    labels = torch.arange(n) % c
+    labels[ids] = torch.arange(c)
+    v = (labels.view(1, 1, n, 1) * 4 + torch.randn(2, 2, n, dim, generator=g) * .01).to(dtype)
+    perm, lab, centers = ops.group_values(v.cuda(), count, iterations, debug=True)
+    e_lab, e_centers = O.lloyd_fp64(v.float().numpy(), count, iterations)
+    assert np.array_equal(_np(lab), e_lab)
+    assert np.array_equal(_np(perm), O.stable_argsort(e_lab))
+    np.testing.assert_allclose(_np(centers), e_centers, rtol=2e-5, atol=2e-6)
+
+
+def test_group_values_stable_known_answer_and_constant(ops):
+    labels = torch.tensor([2, 0, 1, 2, 1, 0])
+    values = labels.float().reshape(1, 1, 6, 1).expand(2, 2, 6, 64).contiguous()
+    perm = ops.group_values(values.cuda(), 3, 2)
+    for p in _np(perm).reshape(-1, 6):
+        assert p.tolist() == [0, 3, 2, 4, 1, 5]
+    v = torch.full((2, 2, 257, 128), 2.)
+    perm, lab, centers = ops.group_values(v.cuda(), 8, 3, debug=True)
+    assert int(lab.count_nonzero()) == 0
+    assert torch.equal(perm.cpu(), torch.arange(257).expand(2, 2, 257))
+    assert bool((centers == 2).all())
+
+
+def _device_state(ops, q, k, v, *, expcast=True, v_smooth=False, v_scale_mode="channel", perm=None):
+    """Prepare payloads on the GPU (bit-exact with the oracle) as a state dict."""
+    qc, kc, vc = q.cuda(), k.cuda(), v.cuda()
+    pc = perm.cuda() if perm is not None else None
+    q8, qs, k8, ks, km = ops.prep_qk_int8(qc, kc, perm=pc)
+    if v_smooth:
+        v8, vs, means = ops.prep_v_blocks(vc, perm=pc, channel_scale=v_scale_mode == "channel")
+    else:
+        v8, vs = ops.prep_v_channel(vc)
+        means = torch.empty(0, dtype=torch.float16, device="cuda")
+    return {"q": q8, "k": k8, "v": v8, "qs": qs, "ks": ks, "vs": vs, "means": means, "expcast": expcast,
+            "block_values": v_smooth, "scale": q.shape[-1] ** -0.5, "km": km}
+
+
+def _cpu_state(st):
+    return {**{k: (v.cpu() if torch.is_tensor(v) else v) for k, v in st.items()},
+            "v": _np(st["v"].view(torch.uint8)), "means": _np(st["means"]) if st["block_values"] else None}
+
+
+ATT_CASES = [
+    # name, shape, dtype, koff, expcast, v_smooth, v_scale_mode
+    ("c1_d128_fp32", (1, 2, 1024, 128), torch.float32, 2 ** 0.5, True, False, "channel"),
+    ("tail_d64_bf16", (1, 2, 300, 64), torch.bfloat16, 3 ** 0.5, True, False, "channel"),
+    ("tail_d128_fp16", (2, 1, 333, 128), torch.float16, 1.0, True, False, "channel"),
+    ("single_key", (1, 1, 1, 128), torch.bfloat16, 0.0, True, False, "channel"),
+    ("smooth_channel", (1, 2, 300, 128), torch.bfloat16, 3 ** 0.5, True, True, "channel"),
+    ("smooth_block_d64", (2, 1, 257, 64), torch.float16, 1.0, True, True, "block"),
+    ("control_no_expcast", (1, 1, 129, 128), torch.bfloat16, 1.0, False, False, "channel"),
+    ("control_smooth", (1, 1, 260, 64), torch.bfloat16, 1.0, False, True, "channel"),
+]
+
+
+@pytest.mark.parametrize("name,shape,dtype,koff,expcast,v_smooth,vmode", ATT_CASES)
+def test_attention_matches_oracle(ops, name, shape, dtype, koff, expcast, v_smooth, vmode):
+    q, k, v = qk_inputs(21, shape, dtype, koff)
+    perm = None
+    if v_smooth:
+        v = mixture_values(21, shape, dtype)
+        perm = ops.group_values(v.cuda(), 8, 2).cpu()
+    st = _device_state(ops, q, k, v, expcast=expcast, v_smooth=v_smooth, v_scale_mode=vmode, perm=perm)
+    out = ops.attention_fwd(st["q"], st["qs"], st["k"], st["ks"], st["v"], st["vs"], st["means"],
+                            out_dtype=torch.float32, sm_scale=st["scale"], expcast=expcast, block_values=v_smooth)
+    torch.cuda.synchronize()
+    ref = O.reference(_cpu_state(st))
+    m = O.metrics(out.cpu(), ref)
+    assert m["cos"] >= COS_MIN and m["rel_l2"] <= REL_MAX, m
+
+
+@pytest.mark.parametrize("name", ["c1_expcast", "tail_expcast_d64", "smooth_channel", "smooth_block_d64",
+                                  "control_no_expcast"])
+def test_attention_matches_reference_oracle_fixture(ops, name):
+    """End to end against outputs of the reference's own vc_reference.reference."""
+    f = np.load(GOLDEN / f"att_{name}.npz")
+    dtype = getattr(torch, str(f["dtype"]))
+    shape = tuple(f["shape"])
+    q, k, v = qk_inputs(int(f["seed"]), shape, dtype, float(f["koff"]))
+    smooth = bool(f["v_smooth"])
+    if smooth:
+        v = mixture_values(int(f["seed"]), shape, dtype)
+    perm = torch.from_numpy(f["permutation"]) if smooth else None
+    # km of the fixture came from torch's CPU mean; use the same for bit-exact payloads
+    kk = k.gather(2, perm.unsqueeze(-1).expand_as(k)) if smooth else k
+    km = O.k_mean(kk).cuda()
+    qc, kc, vc = q.cuda(), k.cuda(), v.cuda()
+    pc = perm.cuda() if smooth else None
+    q8, qs, k8, ks, _ = ops.prep_qk_int8(qc, kc, perm=pc, km=km)
+    if smooth:
+        v8, vs, means = ops.prep_v_blocks(vc, perm=pc, channel_scale=str(f["v_scale_mode"]) == "channel")
+    else:
+        v8, vs = ops.prep_v_channel(vc)
+        means = None
+    out = ops.attention_fwd(q8, qs, k8, ks, v8, vs, means, out_dtype=torch.float32, expcast=bool(f["expcast"]),
+                            block_values=smooth)
+    m = O.metrics(out.cpu(), torch.from_numpy(f["out"]))
+    assert m["cos"] >= COS_MIN and m["rel_l2"] <= REL_MAX, m
+
+
+def test_attention_sharded_units_cover_output(ops):
+    shape = (2, 3, 300, 128)
+    q, k, v = qk_inputs(5, shape, torch.bfloat16, 1.0)
+    st = _device_state(ops, q, k, v)
+    full = ops.attention_fwd(st["q"], st["qs"], st["k"], st["ks"], st["v"], st["vs"], None)
+    units = 2 * 3 * 3
+    out = torch.zeros_like(full)
+    for b, e in ((0, 5), (5, 11), (11, units)):
+        ops.attention_fwd(st["q"], st["qs"], st["k"], st["ks"], st["v"], st["vs"], None, out=out, unit_range=(b, e))
+    assert torch.equal(out, full)
+
+
+def test_sageattn_vc_end_to_end_and_nhd(ops):
+    from sageattention_local import sageattn_vc
+    shape = (1, 2, 520, 128)
+    q, k, v = qk_inputs(7, shape, torch.bfloat16, 3 ** 0.5)
+    out = sageattn_vc(q.cuda(), k.cuda(), v.cuda(), v_smooth=False)
+    assert out.dtype == torch.bfloat16 and out.shape == q.shape
+    st = O.prepare(q, k, v, v_smooth=False, km=O.k_mean(k))
+    ref = O.reference(st)
+    m = O.metrics(out.float().cpu(), ref)
+    assert m["cos"] >= 0.9999 and m["rel_l2"] <= 4e-3, m    # bf16 output rounding included
+    nhd = sageattn_vc(*(x.cuda().transpose(1, 2).contiguous() for x in (q, k, v)), tensor_layout="NHD",
+                      v_smooth=False)
+    assert torch.equal(nhd.transpose(1, 2), out)
+    dense = O.dense_attention(q, k, v)
+    print("vs dense fp32:", O.metrics(out.float().cpu(), dense))
+
+
+def test_sageattn_vc_smooth_end_to_end(ops):
+    from sageattention_local import sageattn_vc
+    shape = (1, 2, 400, 64)
+    q, k, _ = qk_inputs(8, shape, torch.float16, 1.0)
+    v = mixture_values(8, shape, torch.float16)
+    out = sageattn_vc(q.cuda(), k.cuda(), v.cuda(), v_smooth=True)
+    dense = O.dense_attention(q, k, v)
+    m = O.metrics(out.float().cpu(), dense)
+    assert m["rel_l2"] < 0.08, m
