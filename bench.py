@@ -186,8 +186,12 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--gather", action="store_true", help="also time the optional NCCL all-gather of outputs")
+    ap.add_argument("--shape", default=None, help="B,H,S,D override of the config shape (profiling cases)")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
+    if args.shape:
+        b_, h_, s_, d_ = (int(x) for x in args.shape.split(","))
+        cfg = (b_, h_, s_, d_, *cfg[4:7], f"BNSD [{b_},{h_},{s_},{d_}] ({args.config} settings)")
     if args.impl == "reference":
         run_reference(args, cfg)
         return

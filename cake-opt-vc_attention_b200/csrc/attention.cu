@@ -32,6 +32,8 @@
 // All device waits are bounded; on timeout the kernel records an error bit
 // and unwinds instead of hanging.
 #include <cuda.h>
+#include <cstdlib>
+#include <cstring>
 #include "common.cuh"
 #include "kernels.h"
 
@@ -433,6 +435,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+#include "attention_fast.cuh"
+
 // ---------------------------------------------------------------------------
 // Host side: tensor maps and dispatch.
 // ---------------------------------------------------------------------------
@@ -475,9 +479,24 @@ int launch_attn(const AttnArgs& a, const CUtensorMap& mk, const CUtensorMap& mv,
   return cudaGetLastError() == cudaSuccess ? VC_OK : VC_ERR_LAUNCH;
 }
 
+bool force_general() {
+  const char* e = getenv("VC_B200_KERNEL");
+  return e && strcmp(e, "general") == 0;
+}
+
+template <int D, typename OutT>
+int launch_fast(const CUtensorMap& mk, const CUtensorMap& mv, const Params& p, int64_t units, cudaStream_t st) {
+  auto k = vc_attention_fast_kernel<D, OutT>;
+  const int smem = FastSmem<D>::kAlloc;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return VC_ERR_LAUNCH;
+  k<<<static_cast<unsigned>(units), kFastThreads, smem, st>>>(mk, mv, p);
+  return cudaGetLastError() == cudaSuccess ? VC_OK : VC_ERR_LAUNCH;
+}
+
 template <int D, typename OutT>
 int dispatch_flags(const AttnArgs& a, const CUtensorMap& mk, const CUtensorMap& mv, const Params& p, int64_t units,
                    cudaStream_t st) {
+  if (a.expcast && !a.block_values && !force_general()) return launch_fast<D, OutT>(mk, mv, p, units, st);
   if (a.expcast) {
     if (!a.block_values) return launch_attn<D, OutT, true, false, false>(a, mk, mv, p, units, st);
     if (a.vs_per_block) return launch_attn<D, OutT, true, true, true>(a, mk, mv, p, units, st);

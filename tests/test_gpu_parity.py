@@ -248,6 +248,37 @@ def test_attention_matches_reference_oracle_fixture(ops, name):
     assert m["cos"] >= COS_MIN and m["rel_l2"] <= REL_MAX, m
 
 
+@pytest.mark.parametrize("shape", [(1, 2, 1000, 128), (2, 1, 385, 64), (1, 1, 130, 128)])
+def test_fast_and_general_kernels_agree_with_oracle(ops, monkeypatch, shape):
+    """The TMEM-accumulating fast kernel and the register-accumulating general
+    kernel both meet the tolerance on the same payloads."""
+    q, k, v = qk_inputs(31, shape, torch.bfloat16, 3 ** 0.5)
+    st = _device_state(ops, q, k, v)
+    args = (st["q"], st["qs"], st["k"], st["ks"], st["v"], st["vs"], None)
+    fast = ops.attention_fwd(*args, out_dtype=torch.float32)
+    monkeypatch.setenv("VC_B200_KERNEL", "general")
+    general = ops.attention_fwd(*args, out_dtype=torch.float32)
+    monkeypatch.delenv("VC_B200_KERNEL")
+    ref = O.reference(_cpu_state(st))
+    for out in (fast, general):
+        m = O.metrics(out.cpu(), ref)
+        assert m["cos"] >= COS_MIN and m["rel_l2"] <= REL_MAX, m
+
+
+def test_attention_large_logits_and_rescales(ops):
+    """Strongly peaked rows (large scale) force frequent max changes and
+    saturated ExpCast bytes; outputs stay within tolerance."""
+    shape = (1, 2, 700, 128)
+    q, k, v = qk_inputs(32, shape, torch.bfloat16, 3 ** 0.5)
+    st = _device_state(ops, q, k, v)
+    for scale in (2.0, 0.01):
+        out = ops.attention_fwd(st["q"], st["qs"], st["k"], st["ks"], st["v"], st["vs"], None,
+                                out_dtype=torch.float32, sm_scale=scale)
+        ref = O.reference({**_cpu_state(st), "scale": scale})
+        m = O.metrics(out.cpu(), ref)
+        assert m["cos"] >= COS_MIN and m["rel_l2"] <= REL_MAX, (scale, m)
+
+
 def test_attention_sharded_units_cover_output(ops):
     shape = (2, 3, 300, 128)
     q, k, v = qk_inputs(5, shape, torch.bfloat16, 1.0)
