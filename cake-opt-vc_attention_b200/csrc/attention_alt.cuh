@@ -1,0 +1,373 @@
+// Alternating-tile fused attention kernel (ExpCast, channel-scaled V, no
+// block means): the default kernel for that mode.  Included by attention.cu
+// after attention_fast.cuh and attention_pair.cuh (shares their helpers).
+//
+// One CTA owns one 128-row Q tile of a (batch, head).  Warp roles (384 thr):
+//   warps 0-3   softmax group 0: K tiles j = 0, 2, 4, ...
+//   warps 4-7   softmax group 1: K tiles j = 1, 3, 5, ...
+//               thread t owns row t (TMEM lane t) of its tile and the whole
+//               128-key row; the only cross-group dependency is the running
+//               row maximum m_{j-1}, handed over through shared memory with
+//               an mbarrier per tile parity
+//   warp 8      K producer (TMA, 4-deep ring);  warp 10  V producer (3-deep)
+//   warp 9      TMEM allocator + QK^T issuer: QK(j) is issued as soon as K(j)
+//               has landed and the scores of tile j-2 have been read
+//   warp 11     P.V issuer: PV(j) as soon as P(j) and V(j) are ready
+//
+// Tensor memory (496 of 512 columns):
+//   S0 [0,128) S1 [128,256)   s32 scores of tiles j%2
+//   O  [256,256+D+16)         FP32 accumulator for the whole K loop; column D
+//                             accumulates P.1 (the ExpCast denominator) via a
+//                             row of E4M3 1.0 appended to every V tile
+//   P0 [400,432) P1 [432,464) ExpCast bytes of tiles j%2 (A operand of P.V)
+//   Q  [480,480+D/4)          int8 Q tile (A operand of Q.K^T)
+// A group whose rows' maximum grew at tile j scales its lanes of O (and the
+// denominator column) after PV(j-1) completes and before it releases P(j).
+#pragma once
+
+constexpr int kAltThreads = 384;
+constexpr int kKS = 4;   // K ring depth
+constexpr int kVS = 3;   // V ring depth
+constexpr uint32_t kAColS0 = 0, kAColS1 = 128, kAColO = 256, kAColP0 = 400, kAColP1 = 432, kAColQ = 480;
+
+struct __align__(8) AltBarriers {
+  uint64_t k_full[kKS], k_empty[kKS], v_full[kVS], v_empty[kVS];
+  uint64_t q_ready, s_full[2], s_free[2], p_full[2], p_free[2], m_ready[2], o_done, o_final;
+};
+
+template <int D>
+struct AltSmem {
+  static constexpr int kK = 128 * D;
+  static constexpr int kV = (D + 16) * 128;       // V^T rows + ones row + zero rows
+  static constexpr int kOffK = 0;
+  static constexpr int kOffV = kOffK + kKS * kK;
+  static constexpr int kOffM = kOffV + kVS * kV;  // float [2][128] running maxima
+  static constexpr int kOffBar = kOffM + 2 * 128 * 4;
+  static constexpr int kOffSlot = kOffBar + int(sizeof(AltBarriers));
+  static constexpr int kBytes = kOffSlot + 16;
+  static constexpr int kAlloc = kBytes + 1024;
+};
+
+template <int D, typename OutT>
+__global__ void __launch_bounds__(kAltThreads, 1)
+    vc_attention_alt_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                            Params p) {
+  using L = AltSmem<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  AltBarriers* bar = reinterpret_cast<AltBarriers*>(smem + L::kOffBar);
+  float* mbuf = reinterpret_cast<float*>(smem + L::kOffM);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffSlot);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t unit = p.unit_begin + blockIdx.x;
+  const int64_t bh = unit / p.qtiles;
+  const int64_t qt = unit - bh * p.qtiles;
+  const int T = static_cast<int>(p.ktiles);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kKS; ++s) {
+      mbar_init(&bar->k_full[s], 1);
+      mbar_init(&bar->k_empty[s], 1);
+    }
+    for (int s = 0; s < kVS; ++s) {
+      mbar_init(&bar->v_full[s], 1);
+      mbar_init(&bar->v_empty[s], 1);
+    }
+    mbar_init(&bar->q_ready, 128);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar->s_full[b], 1);
+      mbar_init(&bar->s_free[b], 128);
+      mbar_init(&bar->p_full[b], 128);
+      mbar_init(&bar->p_free[b], 1);
+      mbar_init(&bar->m_ready[b], 128);
+    }
+    mbar_init(&bar->o_done, 1);
+    mbar_init(&bar->o_final, 1);
+    fence_barrier_init();
+  }
+  for (int i = threadIdx.x; i < kVS * 16 * 8; i += kAltThreads) {
+    const int s = i / (16 * 8), r = (i / 8) % 16, c = i % 8;
+    const uint32_t fill = r == 0 ? 0x38383838u : 0u;   // E4M3 1.0 in row D, zeros below
+    *reinterpret_cast<uint4*>(smem + L::kOffV + s * L::kV + (D + r) * 128 + c * 16) = make_uint4(fill, fill, fill, fill);
+  }
+  fence_proxy_async_smem();
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  if (warp == 8 && lane == 0) tma_prefetch_desc(&tmk);
+  if (warp == 10 && lane == 0) tma_prefetch_desc(&tmv);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp >= 8) {
+    setmaxnreg_dec<56>();
+    if (warp == 8 && lane == 0) {
+      // ---------------------------------------------------------- K producer
+      for (int j = 0; j < T; ++j) {
+        const int s = j % kKS;
+        if (j >= kKS && !mbar_wait(&bar->k_empty[s], ((j / kKS) & 1) ^ 1, kErrTimeoutProducer)) break;
+        mbar_expect_tx(&bar->k_full[s], L::kK);
+        tma_load_3d(smem + L::kOffK + s * L::kK, &tmk, &bar->k_full[s], 0, j * 128, static_cast<int>(bh));
+      }
+    } else if (warp == 10 && lane == 0) {
+      // ---------------------------------------------------------- V producer
+      for (int j = 0; j < T; ++j) {
+        const int s = j % kVS;
+        if (j >= kVS && !mbar_wait(&bar->v_empty[s], ((j / kVS) & 1) ^ 1, kErrTimeoutProducer)) break;
+        mbar_expect_tx(&bar->v_full[s], D * 128);
+        tma_load_3d(smem + L::kOffV + s * L::kV, &tmv, &bar->v_full[s], j * 128, 0, static_cast<int>(bh));
+      }
+    } else if (warp == 9 && lane == 0) {
+      // ------------------------------------------------------- QK^T issuer
+      // QK(j) goes as soon as K(j) has landed and the scores of tile j-2 have
+      // been read out of S[j%2].
+      constexpr uint32_t idesc_qk = idesc_make(2, 1, 1, 128, 128);     // s32 <- s8 x s8
+      const uint64_t kdesc0 = kmajor_desc<D>(smem_u32(smem + L::kOffK));
+      constexpr uint64_t kStepK = (L::kK >> 4);                         // descriptor start-address units
+      if (mbar_wait(&bar->q_ready, 0, kErrTimeoutMma)) {
+        for (int j = 0; j < T; ++j) {
+          const int s = j % kKS, b = j & 1;
+          if (!mbar_wait(&bar->k_full[s], (j / kKS) & 1, kErrTimeoutMma)) break;
+          if (j >= 2 && !mbar_wait(&bar->s_free[b], ((j - 2) >> 1) & 1, kErrTimeoutMma)) break;
+          tc_fence_after();
+          const uint64_t kd = kdesc0 + s * kStepK;
+          const uint32_t scol = tmem + (b ? kAColS1 : kAColS0);
+#pragma unroll
+          for (int kk = 0; kk < D / 32; ++kk)
+            mma_i8_ts(scol, tmem + kAColQ + kk * 8, kd + 2 * kk, idesc_qk, kk > 0);
+          mma_commit(&bar->k_empty[s]);
+          mma_commit(&bar->s_full[b]);
+        }
+      }
+    } else if (warp == 11 && lane == 0) {
+      // ---------------------------------------------------------- P.V issuer
+      // PV(j) goes as soon as P(j) and V(j) are ready; P has its own TMEM
+      // buffers, so this thread never waits on the QK^T issuer.
+      constexpr uint32_t idesc_pv = idesc_make(1, 0, 0, 128, D + 16);  // f32 <- e4m3 x e4m3
+      const uint64_t vdesc0 = smem_desc_sw128(smem_u32(smem + L::kOffV));
+      constexpr uint64_t kStepV = (L::kV >> 4);
+      bool ok = true;
+      for (int j = 0; j < T && ok; ++j) {
+        const int s = j % kVS, b = j & 1;
+        ok = mbar_wait(&bar->p_full[b], (j >> 1) & 1, kErrTimeoutMma) &&
+             mbar_wait(&bar->v_full[s], (j / kVS) & 1, kErrTimeoutMma);
+        if (!ok) break;
+        tc_fence_after();
+        const uint64_t vd = vdesc0 + s * kStepV;
+        const uint32_t pcol = tmem + (b ? kAColP1 : kAColP0);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_f8_ts(tmem + kAColO, pcol + kk * 8, vd + 2 * kk, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&bar->v_empty[s]);
+        mma_commit(&bar->p_free[b]);
+        mma_commit(&bar->o_done);
+      }
+      if (ok) mma_commit(&bar->o_final);
+    }
+  } else {
+    setmaxnreg_inc<224>();
+    // ------------------------------------------------------------ softmax group w
+    const int w = warp >> 2;
+    const int quarter = warp & 3;
+    const int t = threadIdx.x & 127;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const int64_t row = qt * 128 + t;
+    const bool row_valid = row < p.Sq;
+    if (w == 0) {
+      uint32_t qw[32];
+      const int8_t* qrow = p.q8 + (bh * p.Sq + row) * D;
+#pragma unroll
+      for (int i = 0; i < D / 16; ++i) {
+        uint4 u = row_valid ? __ldg(reinterpret_cast<const uint4*>(qrow) + i) : make_uint4(0, 0, 0, 0);
+        qw[4 * i] = u.x; qw[4 * i + 1] = u.y; qw[4 * i + 2] = u.z; qw[4 * i + 3] = u.w;
+      }
+      if constexpr (D == 128) tmem_st32(tmem + lane_base + kAColQ, qw);
+      else tmem_st16(tmem + lane_base + kAColQ, qw);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bar->q_ready);
+    }
+    const float qscale = row_valid ? p.qs[bh * p.nqs + (row >> 4) * 8 + (row & 7)] : 0.f;
+    const float scale = p.sm_scale;
+    const uint64_t bias2 = pk2f(kBias, kBias), mag2 = pk2f(kMag, kMag);
+    bool ok = true;
+    float4 ksv_next = w < T ? __ldg(reinterpret_cast<const float4*>(p.ks + bh * p.nks + w * 4)) : make_float4(1, 1, 1, 1);
+    for (int j = w; j < T; j += 2) {
+      const int b = j & 1;   // == w
+      const float4 ksv = ksv_next;
+      if (j + 2 < T) ksv_next = __ldg(reinterpret_cast<const float4*>(p.ks + bh * p.nks + (j + 2) * 4));
+      const uint32_t scol = tmem + lane_base + (b ? kAColS1 : kAColS0);
+      ok = mbar_wait_warp(&bar->s_full[b], (j >> 1) & 1, kErrTimeoutSoftmax);
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t raw[128];
+      tmem_ld32(scol + 0, *reinterpret_cast<uint32_t(*)[32]>(raw + 0));
+      tmem_ld32(scol + 32, *reinterpret_cast<uint32_t(*)[32]>(raw + 32));
+      tmem_ld32(scol + 64, *reinterpret_cast<uint32_t(*)[32]>(raw + 64));
+      tmem_ld32(scol + 96, *reinterpret_cast<uint32_t(*)[32]>(raw + 96));
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&bar->s_free[b]);   // QK(j+2) may now overwrite this S buffer
+#pragma unroll
+      for (int c = 0; c < 128; ++c) raw[c] += kBiasBits;
+      if (j == T - 1) {
+        const int valid = static_cast<int>(p.Sk - int64_t(j) * 128);
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (c >= valid) raw[c] = 0xFF800000u;   // -inf: excluded from the max, encodes to 0
+      }
+      const float ksg[4] = {ksv.x, ksv.y, ksv.z, ksv.w};
+      float f1[4];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) f1[g] = __fmul_rn(scale, __fmul_rn(qscale, ksg[g]));
+      float lmax = -__int_as_float(0x7f800000);
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        float mx = max3f(__uint_as_float(raw[2 * g]), __uint_as_float(raw[2 * g + 1]), __uint_as_float(raw[2 * g + 8]));
+        mx = fmaxf(mx, __uint_as_float(raw[2 * g + 9]));
+#pragma unroll
+        for (int k = 2; k < 16; ++k)
+          mx = max3f(mx, __uint_as_float(raw[8 * k + 2 * g]), __uint_as_float(raw[8 * k + 2 * g + 1]));
+        if (mx > 0.f) lmax = fmaxf(lmax, __fmul_rn(__fsub_rn(mx, kBias), f1[g]));
+      }
+      // running maximum handed over from the other group's previous tile
+      float mprev = -5000000.0f;
+      if (j >= 1) {
+        ok = mbar_wait_warp(&bar->m_ready[b ^ 1], ((j - 1) >> 1) & 1, kErrTimeoutSoftmax);
+        if (!ok) break;
+        mprev = mbuf[(b ^ 1) * 128 + t];
+      }
+      const float mn = fmaxf(mprev, lmax);
+      const float alpha = expf(mprev - mn);
+      mbuf[b * 128 + t] = mn;
+      mbar_arrive(&bar->m_ready[b]);
+      uint32_t pw[32];
+      float gain[4];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) gain[g] = __fmul_rn(f1[g], kExpA) * (1.0f / 128.0f);
+      const float cb = __fmaf_rn(-mn, kExpA, kExpB) * (1.0f / 128.0f);
+      const bool safe = !p.exact_expcast && fabsf(mn) <= 128.f && scale >= 1.1754943508222875e-38f &&
+                        isfinite(gain[0]) && isfinite(gain[1]) && isfinite(gain[2]) && isfinite(gain[3]);
+      if (__all_sync(0xffffffffu, safe)) {
+#pragma unroll
+        for (int wd = 0; wd < 32; ++wd) {
+          uint32_t hw[2];
+#pragma unroll
+          for (int q2 = 0; q2 < 2; ++q2) {
+            const int c = 4 * wd + 2 * q2;
+            const int g = (c >> 1) & 3;
+            uint32_t a, bb;
+            up2(f2_sub(pk2(raw[c], raw[c + 1]), bias2), a, bb);
+            const float va = fma_sat(__uint_as_float(a), gain[g], cb);
+            const float vb = fma_sat(__uint_as_float(bb), gain[g], cb);
+            uint32_t wa, wb;
+            up2(f2_add(pk2f(va, vb), mag2), wa, wb);
+            hw[q2] = __byte_perm(wa, wb, 0x0040);
+          }
+          pw[wd] = __byte_perm(hw[0], hw[1], 0x5410);
+        }
+      } else {
+        const uint64_t m2 = pk2f(mn, mn);
+#pragma unroll
+        for (int wd = 0; wd < 32; ++wd) {
+          uint32_t hw[2];
+#pragma unroll
+          for (int q2 = 0; q2 < 2; ++q2) {
+            const int c = 4 * wd + 2 * q2;
+            const int g = (c >> 1) & 3;
+            const uint64_t sh = f2_sub(f2_mul(f2_sub(pk2(raw[c], raw[c + 1]), bias2), pk2f(f1[g], f1[g])), m2);
+            uint32_t a, bb;
+            up2(sh, a, bb);
+            const float va = fma_sat(__uint_as_float(a), kExpA128, kExpB128);
+            const float vb = fma_sat(__uint_as_float(bb), kExpA128, kExpB128);
+            uint32_t wa, wb;
+            up2(f2_add(pk2f(va, vb), mag2), wa, wb);
+            hw[q2] = __byte_perm(wa, wb, 0x0040);
+          }
+          pw[wd] = __byte_perm(hw[0], hw[1], 0x5410);
+        }
+      }
+      // PV(j-2) must be complete before P(j) reuses its buffer -- and before a
+      // parity wait on o_done for PV(j-1) (o_done then lags by at most one phase)
+      if (j >= 2) {
+        ok = mbar_wait_warp(&bar->p_free[b], ((j - 2) >> 1) & 1, kErrTimeoutSoftmax);
+        if (!ok) break;
+      }
+      // rescale O (and the denominator column) between PV(j-1) and PV(j) if any max grew
+      if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+        ok = mbar_wait_warp(&bar->o_done, (j - 1) & 1, kErrTimeoutSoftmax);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t ocol = tmem + lane_base + kAColO;
+#pragma unroll
+        for (int cc = 0; cc < D / 32; ++cc) {
+          uint32_t o[32];
+          tmem_ld32(ocol + cc * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__fmul_rn(__uint_as_float(o[i]), alpha));
+          tmem_st32(ocol + cc * 32, o);
+        }
+        uint32_t o[16];
+        tmem_ld16(ocol + D, o);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__fmul_rn(__uint_as_float(o[i]), alpha));
+        tmem_st16(ocol + D, o);
+      }
+      // P(j) into this group's P buffer (PV(j-2) has consumed it, see above)
+      tc_fence_after();
+      tmem_st32(tmem + lane_base + (b ? kAColP1 : kAColP0), pw);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bar->p_full[b]);
+    }
+    // epilogue: group w writes output channels [w*D/2, (w+1)*D/2)
+    if (ok) ok = mbar_wait_warp(&bar->o_final, 0, kErrTimeoutSoftmax);
+    if (ok) {
+      tc_fence_after();
+      uint32_t dn[16];
+      tmem_ld16(tmem + lane_base + kAColO + D, dn);
+      tmem_wait_ld();
+      const float denom = __uint_as_float(dn[0]);
+      OutT* orow = reinterpret_cast<OutT*>(p.out) + (bh / p.H) * p.osb + (bh % p.H) * p.osh + row * p.oss;
+#pragma unroll
+      for (int cc = 0; cc < D / 64; ++cc) {
+        const int cbase = w * (D / 2) + cc * 32;
+        uint32_t o[32];
+        tmem_ld32(tmem + lane_base + kAColO + cbase, o);
+        tmem_wait_ld();
+        if (row_valid) {
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8) {
+            const int c0 = cbase + c8 * 8;
+            const float4 vsa = __ldg(reinterpret_cast<const float4*>(p.vs + bh * D + c0));
+            const float4 vsb = __ldg(reinterpret_cast<const float4*>(p.vs + bh * D + c0 + 4));
+            const float vsv[8] = {vsa.x, vsa.y, vsa.z, vsa.w, vsb.x, vsb.y, vsb.z, vsb.w};
+            float ov[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ov[i] = __fmul_rn(__fdiv_rn(__uint_as_float(o[c8 * 8 + i]), denom), vsv[i]);
+            constexpr int kWords = 8 * int(sizeof(OutT)) / 16;
+            uint4 u[kWords];
+            OutT* h = reinterpret_cast<OutT*>(u);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) h[i] = to_out<OutT>(ov[i]);
+#pragma unroll
+            for (int ww = 0; ww < kWords; ++ww) reinterpret_cast<uint4*>(orow + c0)[ww] = u[ww];
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}

@@ -236,16 +236,18 @@ __global__ void __launch_bounds__(kFastThreads, 1)
     const int key0 = half * 64;
     float m = -5000000.0f;
     bool ok = true;
+    float4 ksv_next = __ldg(reinterpret_cast<const float4*>(p.ks + bh * p.nks));
     for (int j = 0; j < T; ++j) {
       const int b = j & 1;
       const uint32_t sbase = b ? kFColS1 : kFColS0;
+      const float4 ksv = ksv_next;
+      if (j + 1 < T) ksv_next = __ldg(reinterpret_cast<const float4*>(p.ks + bh * p.nks + (j + 1) * 4));
       ok = mbar_wait_warp(&bar->s_full[b], (j >> 1) & 1, kErrTimeoutSoftmax);
       if (!ok) break;
       tc_fence_after();
       uint32_t raw[64];
       tmem_ld32(tmem + lane_base + sbase + key0, *reinterpret_cast<uint32_t(*)[32]>(raw + 0));
       tmem_ld32(tmem + lane_base + sbase + key0 + 32, *reinterpret_cast<uint32_t(*)[32]>(raw + 32));
-      const float4 ksv = __ldg(reinterpret_cast<const float4*>(p.ks + bh * p.nks + j * 4));
       tmem_wait_ld();
 #pragma unroll
       for (int c = 0; c < 64; ++c) raw[c] += kBiasBits;
@@ -278,26 +280,57 @@ __global__ void __launch_bounds__(kFastThreads, 1)
       const float mn = fmaxf(m, fmaxf(lmax, xch[(b * 2 + (half ^ 1)) * 128 + t]));
       const float alpha = expf(m - mn);
       m = mn;
-      // ExpCast bytes for this half's 64 keys (16 words)
-      const uint64_t bias2 = pk2f(kBias, kBias), m2 = pk2f(mn, mn), mag2 = pk2f(kMag, kMag);
+      // ExpCast bytes for this half's 64 keys (16 words).  Default: the
+      // reference's folded affine encoder (csrc/vc/vc_math.cuh:17-71, 96-106)
+      //   u = fma(float(raw), RN(f1*A), fma(-m', A, B))
+      // used while |m'| <= 128 and the gain is finite; otherwise (and when
+      // the exact mode is requested) the unfused RN(RN(raw*f1) - m') form.
+      const uint64_t bias2 = pk2f(kBias, kBias), mag2 = pk2f(kMag, kMag);
       uint32_t pw[16];
+      float gain[4];
 #pragma unroll
-      for (int w = 0; w < 16; ++w) {
-        uint32_t hw[2];
+      for (int g = 0; g < 4; ++g) gain[g] = __fmul_rn(f1[g], kExpA) * (1.0f / 128.0f);
+      const float cb = __fmaf_rn(-mn, kExpA, kExpB) * (1.0f / 128.0f);
+      const bool safe = !p.exact_expcast && fabsf(mn) <= 128.f && scale >= 1.1754943508222875e-38f &&
+                        isfinite(gain[0]) && isfinite(gain[1]) && isfinite(gain[2]) && isfinite(gain[3]);
+      if (__all_sync(0xffffffffu, safe)) {
 #pragma unroll
-        for (int q2 = 0; q2 < 2; ++q2) {
-          const int c = 4 * w + 2 * q2;
-          const int g = (c >> 1) & 3;
-          const uint64_t sh = f2_sub(f2_mul(f2_sub(pk2(raw[c], raw[c + 1]), bias2), pk2f(f1[g], f1[g])), m2);
-          uint32_t a, bb;
-          up2(sh, a, bb);
-          const float va = fma_sat(__uint_as_float(a), kExpA128, kExpB128);
-          const float vb = fma_sat(__uint_as_float(bb), kExpA128, kExpB128);
-          uint32_t wa, wb;
-          up2(f2_add(pk2f(va, vb), mag2), wa, wb);
-          hw[q2] = __byte_perm(wa, wb, 0x0040);
+        for (int w = 0; w < 16; ++w) {
+          uint32_t hw[2];
+#pragma unroll
+          for (int q2 = 0; q2 < 2; ++q2) {
+            const int c = 4 * w + 2 * q2;
+            const int g = (c >> 1) & 3;
+            uint32_t a, bb;
+            up2(f2_sub(pk2(raw[c], raw[c + 1]), bias2), a, bb);
+            const float va = fma_sat(__uint_as_float(a), gain[g], cb);
+            const float vb = fma_sat(__uint_as_float(bb), gain[g], cb);
+            uint32_t wa, wb;
+            up2(f2_add(pk2f(va, vb), mag2), wa, wb);
+            hw[q2] = __byte_perm(wa, wb, 0x0040);
+          }
+          pw[w] = __byte_perm(hw[0], hw[1], 0x5410);
         }
-        pw[w] = __byte_perm(hw[0], hw[1], 0x5410);
+      } else {
+        const uint64_t m2 = pk2f(mn, mn);
+#pragma unroll
+        for (int w = 0; w < 16; ++w) {
+          uint32_t hw[2];
+#pragma unroll
+          for (int q2 = 0; q2 < 2; ++q2) {
+            const int c = 4 * w + 2 * q2;
+            const int g = (c >> 1) & 3;
+            const uint64_t sh = f2_sub(f2_mul(f2_sub(pk2(raw[c], raw[c + 1]), bias2), pk2f(f1[g], f1[g])), m2);
+            uint32_t a, bb;
+            up2(sh, a, bb);
+            const float va = fma_sat(__uint_as_float(a), kExpA128, kExpB128);
+            const float vb = fma_sat(__uint_as_float(bb), kExpA128, kExpB128);
+            uint32_t wa, wb;
+            up2(f2_add(pk2f(va, vb), mag2), wa, wb);
+            hw[q2] = __byte_perm(wa, wb, 0x0040);
+          }
+          pw[w] = __byte_perm(hw[0], hw[1], 0x5410);
+        }
       }
       // rescale this warp's share of O (after PV(j-1), before PV(j)) if any max grew
       if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {

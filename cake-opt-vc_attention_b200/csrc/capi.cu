@@ -10,8 +10,6 @@
 
 namespace vcb {
 
-__device__ uint32_t g_error_word = 0;
-
 namespace {
 thread_local char t_last_error[512] = "";
 
@@ -122,11 +120,7 @@ int vc_error_read(int device, uint32_t* code, int clear) {
     set_last_error("vc_error_read: bad device %d", device);
     return VC_ERR_ARG;
   }
-  cudaError_t e = cudaMemcpyFromSymbol(code, g_error_word, sizeof(uint32_t));
-  if (e == cudaSuccess && clear) {
-    const uint32_t zero = 0;
-    e = cudaMemcpyToSymbol(g_error_word, &zero, sizeof(uint32_t));
-  }
+  const cudaError_t e = attention_error_word(code, clear != 0);
   cudaSetDevice(prev);
   if (e != cudaSuccess) {
     set_last_error("vc_error_read: %s", cudaGetErrorString(e));
@@ -278,7 +272,8 @@ int vc_attention_fwd(const int8_t* q8, const float* qs, const int8_t* k8, const 
   }
   if (int rc = check_device()) return rc;
   AttnArgs a{q8, qs, k8, ks, v8, vs, means, out, out_dtype, B, H, Sq, Sk, D, out_stride_b, out_stride_h, out_stride_s,
-             expcast ? 1 : 0, block_values ? 1 : 0, vs_per_block ? 1 : 0, sm_scale, unit_begin, unit_end};
+             expcast == 2 ? 2 : (expcast ? 1 : 0), block_values ? 1 : 0, vs_per_block ? 1 : 0, sm_scale, unit_begin,
+             unit_end};
   return finish(fn, attention_fwd(a, static_cast<cudaStream_t>(stream)));
 }
 

@@ -17,9 +17,11 @@ namespace vcb {
 // ---------------------------------------------------------------------------
 // Device error word.  Kernels never trap: a wait that exceeds its budget or a
 // violated device-side invariant ORs a bit in here and the kernel returns.
-// The host reads/clears it with vc_error_read().
+// Each translation unit has its own copy (the library is built without
+// relocatable device code so that ptxas honours setmaxnreg); the units that
+// raise errors export a host reader, combined by vc_error_read().
 // ---------------------------------------------------------------------------
-extern __device__ uint32_t g_error_word;
+static __device__ uint32_t g_error_word = 0;
 
 enum : uint32_t {
   kErrTimeoutTma = 1u << 0,
@@ -133,14 +135,53 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: about (limit * hardware suspend time) before giving up.
-// Returns false (and records ``err``) on timeout; callers then unwind.
-constexpr uint32_t kWaitLimit = 1u << 22;
+// Non-blocking probe (never suspends the thread): for event loops that poll
+// several barriers.
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes or about ``ns`` nanoseconds pass, issuing nothing meanwhile.
+__device__ __forceinline__ bool mbar_try_wait_for(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait: gives up after about two seconds of wall time (far beyond
+// any legitimate wait inside one launch), records ``err`` and returns false;
+// callers then unwind.  The budget is wall time, so it holds whether the
+// hardware honours the suspend hint or returns early.
+constexpr uint64_t kWaitBudgetNs = 2000000000ull;
+constexpr uint32_t kSuspendHintNs = 100000;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t err) {
   const uint32_t a = smem_u32(bar);
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
-    if (mbar_try_wait(a, parity)) return true;
-    if (i > 64) __nanosleep(32);
+  if (mbar_try_wait(a, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait_for(a, parity, kSuspendHintNs)) return true;
+    if (globaltimer_ns() - t0 > kWaitBudgetNs) break;
   }
   raise_error(err);
   return false;
@@ -190,6 +231,14 @@ __device__ __forceinline__ void mma_i8_ts(uint32_t d, uint32_t a, uint64_t bdesc
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
       "r"(a), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// D[tmem] (+)= A[smem desc] * B[smem desc], kind::i8 (s32 accumulate).
+__device__ __forceinline__ void mma_i8_ss(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
       : "memory");
 }
 // D[tmem] (+)= A[tmem] * B[smem desc], kind::f8f6f4 (f32 accumulate).

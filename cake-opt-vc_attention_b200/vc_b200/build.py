@@ -25,7 +25,8 @@ LIB = PKG / "libvc_b200.so"
 OBJ_DIR = ROOT / "_build"
 SOURCES = ["capi.cu", "prep_qk.cu", "prep_v.cu", "cluster.cu", "attention.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-rdc=true", "-Xcompiler", "-fPIC,-O3", "--expt-relaxed-constexpr",
+# Whole-program device code (no -rdc): ptxas honours setmaxnreg only then.
+NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3", "--expt-relaxed-constexpr",
               "-Xptxas", "-v", "-diag-suppress=177"]
 
 
@@ -69,7 +70,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         for _, log in results:
             sys.stderr.write(log)
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc(), *ARCH, "-shared", "-rdc=true", *objs, "-o", str(tmp)]
+    cmd = [nvcc(), *ARCH, "-shared", *objs, "-o", str(tmp)]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stderr[-8000:]}")

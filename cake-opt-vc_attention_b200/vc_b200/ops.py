@@ -165,6 +165,10 @@ def attention_fwd(q8, qs, k8, ks, v8, vs, means, *, out_dtype=torch.bfloat16, sm
                   unit_range: tuple[int, int] | None = None) -> torch.Tensor:
     """Fused attention on prepared payloads.  Returns ``out`` [B,H,Sq,D].
 
+    ``expcast``: True = ExpCast with the reference's folded affine encoder
+    (its default H200 kernel), ``"exact"`` = the unfused decoded-payload
+    contract, False = Sage FP8 probabilities.
+
     ``unit_range`` = [begin, end) over units (b*H+h)*ceil(Sq/128)+q_tile
     computes only that shard (rows outside it are left untouched).
     """
@@ -184,7 +188,8 @@ def attention_fwd(q8, qs, k8, ks, v8, vs, means, *, out_dtype=torch.bfloat16, sm
     with torch.cuda.device(q8.device):
         N.check(lib.vc_attention_fwd(_p(q8), _p(qs), _p(k8), _p(ks), _p(v8.view(torch.uint8)), _p(vs),
                                      _p(means) if block_values else None, _p(out), _DT[out.dtype], B, H, Sq, Sk, D,
-                                     out.stride(0), out.stride(1), out.stride(2), int(expcast), int(block_values),
+                                     out.stride(0), out.stride(1), out.stride(2),
+                                     2 if expcast == "exact" else int(bool(expcast)), int(block_values),
                                      int(vs_per_block), scale, int(ub), int(ue), _stream(q8)), "vc_attention_fwd")
     return out
 

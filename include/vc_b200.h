@@ -120,7 +120,11 @@ int vc_group_values(const void* v, int dtype, int64_t B, int64_t H, int64_t S, i
  * block-mean restoration).  out [B,H,Sq,D] (out_dtype F16, BF16 or F32) through
  * (out_stride_b, out_stride_h, out_stride_s).  Work units are
  * (b*H + h) * ceil(Sq/128) + q_tile; [unit_begin, unit_end) selects a shard
- * (pass 0, -1 for all).  vs_per_block: vs is [B,H,T,D].
+ * (pass 0, -1 for all).  vs_per_block: vs is [B,H,T,D].  expcast: 0 = Sage
+ * FP8 probabilities (control), 1 = ExpCast with the reference's folded affine
+ * encoder (csrc/vc/vc_math.cuh:17-106, exact fallback on extreme ranges),
+ * 2 = ExpCast with the unfused decoded-payload contract
+ * (vc_reference.py:52-54).
  * Replaces _vc_sm90.forward (csrc/vc/vc_sm90.cu:1027-1123, vc_api.h:8-10). */
 int vc_attention_fwd(const int8_t* q8, const float* qs, const int8_t* k8, const float* ks, const uint8_t* v8,
                      const float* vs, const uint16_t* means, void* out, int out_dtype, int64_t B, int64_t H,

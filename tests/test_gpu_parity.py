@@ -256,13 +256,20 @@ def test_fast_and_general_kernels_agree_with_oracle(ops, monkeypatch, shape):
     st = _device_state(ops, q, k, v)
     args = (st["q"], st["qs"], st["k"], st["ks"], st["v"], st["vs"], None)
     fast = ops.attention_fwd(*args, out_dtype=torch.float32)
+    exact = ops.attention_fwd(*args, out_dtype=torch.float32, expcast="exact")
     monkeypatch.setenv("VC_B200_KERNEL", "general")
     general = ops.attention_fwd(*args, out_dtype=torch.float32)
+    monkeypatch.setenv("VC_B200_KERNEL", "split")
+    split = ops.attention_fwd(*args, out_dtype=torch.float32)
+    monkeypatch.setenv("VC_B200_KERNEL", "pair")
+    pair = ops.attention_fwd(*args, out_dtype=torch.float32)
     monkeypatch.delenv("VC_B200_KERNEL")
     ref = O.reference(_cpu_state(st))
-    for out in (fast, general):
+    for out in (fast, exact, general, split, pair):
         m = O.metrics(out.cpu(), ref)
         assert m["cos"] >= COS_MIN and m["rel_l2"] <= REL_MAX, m
+    # the exact encoder reproduces the oracle's bytes: only accumulation order differs
+    assert O.metrics(exact.cpu(), ref)["rel_l2"] <= 2e-5
 
 
 def test_attention_large_logits_and_rescales(ops):
