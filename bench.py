@@ -74,7 +74,12 @@ def gen_head(bh: int, S: int, D: int, dtype, k_std: float, smooth: bool, device,
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks / throttle reasons, sampled every 100 ms with host
+    timestamps.  ``start()`` waits for the first sample so that sampling is
+    live before the timed region; ``mark(t0, t1)`` records the timed region's
+    host-time window.  The summary uses the samples inside that window, and
+    when it is shorter than three sample periods, the window from the start
+    of the warm-up (same kernels, same load) as well, saying which."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -83,35 +88,47 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
-        self.lines = []
+        self.samples = []          # (host time, csv line)
+        self.window = None
+        self.t_warm = None
 
-    def __enter__(self):
+    def start(self, wait_s: float = 10.0):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
         except (FileNotFoundError, OSError):
             self.proc = None
+            return self
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+        t_end = time.time() + wait_s
+        while not self.samples and time.time() < t_end and self.proc.poll() is None:
+            time.sleep(0.01)
+        self.t_warm = time.time()
         return self
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.samples.append((time.time(), line.strip()))
 
-    def __exit__(self, *exc):
+    def mark(self, t0: float, t1: float):
+        self.window = (t0, t1)
+
+    def stop(self):
         if self.proc is not None:
+            time.sleep(0.15)       # let the sample that covers the window's end arrive
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
 
-    def summary(self):
+    @staticmethod
+    def _parse(lines):
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -123,10 +140,23 @@ class ClockSampler:
             for n, val in zip(names, parts[5:9]):
                 if val.lower() == "active":
                     reasons.add(n)
-        if not sm:
+        return sm, mx, reasons
+
+    def summary(self):
+        if not self.window:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        t0, t1 = self.window
+        period = 0.1
+        inside = [ln for t, ln in self.samples if t0 <= t <= t1 + period]
+        scope = "timed region"
+        if len(inside) < 3 and self.t_warm is not None:
+            inside = [ln for t, ln in self.samples if self.t_warm <= t <= t1 + period]
+            scope = "warm-up + timed region (timed region alone is under 3 sample periods)"
+        sm, mx, reasons = self._parse(inside)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "scope": scope}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "scope": scope}
 
 
 def cpu_baseline_sample(B, H, S, D, dtype, k_std, smooth, threads=None):
@@ -179,7 +209,7 @@ def run_reference(args, cfg):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--config", choices=tuple(CONFIGS), default="c2")
@@ -241,23 +271,25 @@ def main():
             e1.record()
             att_events.append((e0, e1))
 
+    clocks = ClockSampler(local).start()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    clocks = ClockSampler(local)
-    with clocks:
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        if dist:
-            dist.barrier()
-        t0.record()
-        for _ in range(args.steps):
-            step(record=True)
-        t1.record()
-        torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    h0 = time.time()
+    t0.record()
+    for _ in range(args.steps):
+        step(record=True)
+    t1.record()
+    torch.cuda.synchronize()
+    clocks.mark(h0, time.time())
+    clocks.stop()
     ms = t0.elapsed_time(t1) / args.steps
     att_ms = statistics.mean(a.elapsed_time(b) for a, b in att_events)
     if dist:
