@@ -97,6 +97,36 @@ int expcast_codes(const float* x, uint8_t* y, int64_t n, cudaStream_t st) {
   return cudaGetLastError() == cudaSuccess ? VC_OK : VC_ERR_LAUNCH;
 }
 
+// Library-owned scratch for vc_prep_v_channel_static: the per-channel amax
+// words (B*H*D uint32).  One array per device, shared by every call on that
+// device; each call zeroes the words it uses on its own stream first.
+static __device__ __align__(256) uint32_t g_static_scratch[VC_STATIC_SCRATCH_BYTES / 4];
+
+namespace {
+// Device address of g_static_scratch on the current device, resolved once per
+// device (cudaGetSymbolAddress with that device current) and cached.
+void* static_scratch() {
+  static std::mutex mu;
+  static void* cache[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    set_last_error("no current CUDA device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cache[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess || !p) {
+      set_last_error("cudaGetSymbolAddress(static scratch) failed on device %d: %s", dev, cudaGetErrorString(e));
+      return nullptr;
+    }
+    cache[dev] = p;
+  }
+  return cache[dev];
+}
+}  // namespace
+
 }  // namespace vcb
 
 using namespace vcb;
@@ -186,6 +216,30 @@ int vc_prep_v_channel(const void* v, int dtype, int64_t B, int64_t H, int64_t S,
   }
   if (int rc = check_device()) return rc;
   PrepVArgs a{v, dtype, B, H, S, D, stride_b, stride_h, stride_s, perm, 1, 1, v8, vs, nullptr, workspace};
+  return finish(fn, prep_v_channel(a, static_cast<cudaStream_t>(stream)));
+}
+
+int vc_prep_v_channel_static(const void* v, int dtype, int64_t B, int64_t H, int64_t S, int64_t D,
+                             int64_t stride_b, int64_t stride_h, int64_t stride_s, const int64_t* perm, uint8_t* v8,
+                             float* vs, void* stream) {
+  const char* fn = "vc_prep_v_channel_static";
+  if (int rc = check_common(fn, dtype, B, H, S, D)) return rc;
+  if (int rc = check_input(fn, "v", v, dtype, stride_b, stride_h, stride_s)) return rc;
+  if (!v8 || !vs || !aligned16(v8) || !aligned16(vs)) {
+    set_last_error("%s: v8/vs must be non-null and 16-byte aligned", fn);
+    return VC_ERR_ARG;
+  }
+  const int64_t need = B * H * D * 4;   // amax words, zeroed by the launcher before use
+  if (need > VC_STATIC_SCRATCH_BYTES) {
+    set_last_error("%s: needs %lld bytes of scratch (B*H*D*4) but the static array holds %d (B*H*D <= %d); "
+                   "use vc_prep_v_channel with a caller workspace",
+                   fn, (long long)need, VC_STATIC_SCRATCH_BYTES, VC_STATIC_SCRATCH_BYTES / 4);
+    return VC_ERR_WORKSPACE;
+  }
+  if (int rc = check_device()) return rc;
+  void* scratch = static_scratch();
+  if (!scratch) return VC_ERR_LAUNCH;
+  PrepVArgs a{v, dtype, B, H, S, D, stride_b, stride_h, stride_s, perm, 1, 1, v8, vs, nullptr, scratch};
   return finish(fn, prep_v_channel(a, static_cast<cudaStream_t>(stream)));
 }
 

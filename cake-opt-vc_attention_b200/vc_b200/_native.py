@@ -29,6 +29,7 @@ SIGNATURES = {
                                _p, _p, _p, _i64, _i64, _p, _p, _p, _p, _p, _i64, _p]),
     "vc_prep_v_channel_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64]),
     "vc_prep_v_channel": (_i32, [_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _p]),
+    "vc_prep_v_channel_static": (_i32, [_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p]),
     "vc_prep_v_blocks_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64]),
     "vc_prep_v_blocks": (_i32, [_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i32, _i32, _p, _p, _p, _p,
                                 _i64, _p]),

@@ -88,6 +88,26 @@ int vc_prep_v_channel(const void* v, int dtype, int64_t B, int64_t H, int64_t S,
                       int64_t stride_h, int64_t stride_s, const int64_t* perm, uint8_t* v8, float* vs,
                       void* workspace, int64_t workspace_bytes, void* stream);
 
+/* vc_prep_v_channel without a caller workspace, for callers that cannot
+ * allocate device memory.  It has no counterpart in the reference.
+ * Same arguments, results and errors as vc_prep_v_channel; its scratch (the
+ * per-channel amax words, B*H*D*4 bytes) lives in a library-owned static
+ * device array of VC_STATIC_SCRATCH_BYTES (1 MiB), so B*H*D must not exceed
+ * 262144 (e.g. B*H <= 2048 at D = 128); larger sizes return VC_ERR_WORKSPACE
+ * and launch nothing.  It allocates nothing: no cudaMalloc, no cudaFree.
+ *   - The first call on each device (that device current) resolves the
+ *     array's device address once (cudaGetSymbolAddress); make that first
+ *     call before any stream capture on that device.
+ *   - Every call on a device shares the one array.  Each call zeroes the
+ *     words it uses on ``stream`` before its kernels read them, so calls in
+ *     stream order are independent; calls that overlap on the GPU (other
+ *     streams, other host threads without ordering) race on the array and
+ *     must be serialised by the caller. */
+#define VC_STATIC_SCRATCH_BYTES (1 << 20)
+int vc_prep_v_channel_static(const void* v, int dtype, int64_t B, int64_t H, int64_t S, int64_t D,
+                             int64_t stride_b, int64_t stride_h, int64_t stride_s, const int64_t* perm, uint8_t* v8,
+                             float* vs, void* stream);
+
 /* Smoothed V: 128-token block de-meaning, E4M3 residual, FP16 mean/scale.
  * channel_scale=1: vs [B,H,D]; 0: vs [B,H,T,D] (per block).  demean=0 keeps
  * the block mean at zero (per-block amax scaling only, the Config-API
