@@ -308,10 +308,16 @@ def main():
     hbm, bf16, bf16_sus, basis = peaks()
     peak_tops = 2.0 * bf16          # dense INT8/FP8 tensor rate is 2x the measured dense BF16 rate
     achieved = ops_launch / (att_ms * 1e-3) / 1e12
+    # DRAM bytes per launch: dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of the
+    # alternating-tile kernel on a 6-head slice of config 2 (116.4 MB), scaled by the heads in this
+    # launch (profiles/vc_attention_alt_kernel_1x6x37741.txt); D128, ExpCast, channel-scaled V only.
+    traffic = None
+    if D == 128 and not smooth and S == 37741:
+        traffic = 116.44e6 / 6 * nbh
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_tops, "unit": "TFLOP/s",
-                "frac": achieved / peak_tops, "traffic": None,
-                "kernel": "vc_attention_kernel", "peak_basis": f"2 x bf16_tflops ({basis}, MEASURED_PEAKS.json)",
-                "kernel_ms": att_ms}
+                "frac": achieved / peak_tops, "traffic": traffic,
+                "kernel": "vc_attention_alt_kernel", "peak_basis": f"2 x bf16_tflops ({basis}, MEASURED_PEAKS.json)",
+                "kernel_ms": att_ms, "algorithmic_ops_per_launch": ops_launch}
 
     # end to end through the public API with pinned host buffers
     e2e = None

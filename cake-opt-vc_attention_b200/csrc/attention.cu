@@ -600,14 +600,7 @@ int attention_fwd(const AttnArgs& a, cudaStream_t st) {
   return a.D == 128 ? dispatch_flags<128, __half>(a, m, p, units, st) : dispatch_flags<64, __half>(a, m, p, units, st);
 }
 
-cudaError_t attention_error_word(uint32_t* code, bool clear) {
-  cudaError_t e = cudaMemcpyFromSymbol(code, g_error_word, sizeof(uint32_t));
-  if (e == cudaSuccess && clear) {
-    const uint32_t zero = 0;
-    e = cudaMemcpyToSymbol(g_error_word, &zero, sizeof(uint32_t));
-  }
-  return e;
-}
+cudaError_t attention_error_word(uint32_t* code, bool clear) { return read_tu_error_word(code, clear); }
 
 int attention_resources(int head_dim, int64_t* out4) {
   cudaFuncAttributes fa;

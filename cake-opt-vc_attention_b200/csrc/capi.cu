@@ -150,7 +150,11 @@ int vc_error_read(int device, uint32_t* code, int clear) {
     set_last_error("vc_error_read: bad device %d", device);
     return VC_ERR_ARG;
   }
-  const cudaError_t e = attention_error_word(code, clear != 0);
+  uint32_t words[3] = {0, 0, 0};
+  cudaError_t e = attention_error_word(&words[0], clear != 0);
+  if (e == cudaSuccess) e = prep_qk_error_word(&words[1], clear != 0);
+  if (e == cudaSuccess) e = prep_v_error_word(&words[2], clear != 0);
+  *code = words[0] | words[1] | words[2];
   cudaSetDevice(prev);
   if (e != cudaSuccess) {
     set_last_error("vc_error_read: %s", cudaGetErrorString(e));

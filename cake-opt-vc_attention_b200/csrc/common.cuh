@@ -31,9 +31,21 @@ enum : uint32_t {
   kErrTimeoutProducer = 1u << 4,
   kErrTmemAlloc = 1u << 5,
   kErrBadArgument = 1u << 6,
+  kErrBadIndex = 1u << 7,     // a permutation entry outside [0, S): that row read as zeros
 };
 
 __device__ __forceinline__ void raise_error(uint32_t bits) { atomicOr(&g_error_word, bits); }
+
+// Host: copy (and optionally clear) this translation unit's error word on the
+// current device.  Synchronous.
+static inline cudaError_t read_tu_error_word(uint32_t* code, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(code, g_error_word, sizeof(uint32_t));
+  if (e == cudaSuccess && clear) {
+    const uint32_t zero = 0;
+    e = cudaMemcpyToSymbol(g_error_word, &zero, sizeof(uint32_t));
+  }
+  return e;
+}
 
 __host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 

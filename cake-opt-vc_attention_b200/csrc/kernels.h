@@ -75,9 +75,11 @@ struct AttnArgs {
   int64_t unit_begin, unit_end;
 };
 int attention_fwd(const AttnArgs& a, cudaStream_t st);
-// Copy (and optionally clear) the attention kernels' device error word of the
+// Copy (and optionally clear) the device error word of each kernel file on the
 // current device.  Synchronous.
 cudaError_t attention_error_word(uint32_t* code, bool clear);
+cudaError_t prep_qk_error_word(uint32_t* code, bool clear);
+cudaError_t prep_v_error_word(uint32_t* code, bool clear);
 int attention_resources(int head_dim, int64_t* out4);
 
 int expcast_codes(const float* x, uint8_t* y, int64_t n, cudaStream_t st);

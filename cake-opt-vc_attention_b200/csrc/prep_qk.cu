@@ -166,7 +166,13 @@ __global__ void __launch_bounds__(128) quant_k(const T* __restrict__ k, int64_t 
     if (row < S) {
       const int64_t src = perm ? perm[bh * S + row] : row;
       float raw[E];
-      load_vec<T, E>(row_ptr(k, bh, H, sb, sh, ss, src) + col, raw);
+      if (src >= 0 && src < S) {
+        load_vec<T, E>(row_ptr(k, bh, H, sb, sh, ss, src) + col, raw);
+      } else {
+        raise_error(kErrBadIndex);   // out-of-range permutation entry: the row reads as zeros
+#pragma unroll
+        for (int j = 0; j < E; ++j) raw[j] = 0.f;
+      }
 #pragma unroll
       for (int j = 0; j < E; ++j) {
         x[i][j] = round_as(__fsub_rn(raw[j], kmv[j]), static_cast<T*>(nullptr));
@@ -235,5 +241,7 @@ int prep_qk(const PrepQKArgs& a, cudaStream_t st) {
 #undef VCB_QK
   return VC_ERR_ARG;
 }
+
+cudaError_t prep_qk_error_word(uint32_t* code, bool clear) { return read_tu_error_word(code, clear); }
 
 }  // namespace vcb

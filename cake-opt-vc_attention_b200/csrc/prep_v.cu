@@ -39,7 +39,10 @@ __device__ __forceinline__ void stage_tile(uint8_t* sin, const T* __restrict__ v
     uint4 val = make_uint4(0, 0, 0, 0);
     if (row < S) {
       const int64_t src = perm ? perm[bh * S + row] : row;
-      val = __ldg(reinterpret_cast<const uint4*>(base + src * ss) + c);
+      if (src >= 0 && src < S)
+        val = __ldg(reinterpret_cast<const uint4*>(base + src * ss) + c);
+      else
+        raise_error(kErrBadIndex);
     }
     *reinterpret_cast<uint4*>(sin + r * G::kPitch + c * 16) = val;
   }
@@ -292,5 +295,7 @@ int64_t prep_v_blocks_workspace(int64_t B, int64_t H, int64_t S, int64_t D) {
 int prep_v_channel(const PrepVArgs& a, cudaStream_t st) { VCB_DISPATCH_V(launch_v_channel) }
 int prep_v_blocks(const PrepVArgs& a, cudaStream_t st) { VCB_DISPATCH_V(launch_v_blocks) }
 #undef VCB_DISPATCH_V
+
+cudaError_t prep_v_error_word(uint32_t* code, bool clear) { return read_tu_error_word(code, clear); }
 
 }  // namespace vcb

@@ -38,6 +38,18 @@ def _rowmajor(x: torch.Tensor) -> torch.Tensor:
     return x.contiguous()
 
 
+def _perm(name, perm, B, H, S):
+    """Per-(batch, head) token permutation: [B, H, S] integers, made int64
+    contiguous.  Entries must lie in [0, S); the kernels record an error bit
+    and read zeros for any that do not."""
+    if perm is None:
+        return None
+    if tuple(perm.shape) != (B, H, S) or perm.dtype.is_floating_point or perm.dtype == torch.bool:
+        raise ValueError(f"{name}: perm must be an integer tensor of shape {(B, H, S)}, got "
+                         f"{tuple(perm.shape)} {perm.dtype}")
+    return perm.to(torch.int64).contiguous()
+
+
 def _workspace(nbytes: int, device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device)
 
@@ -76,8 +88,7 @@ def prep_qk_int8(q: torch.Tensor, k: torch.Tensor, *, perm: torch.Tensor | None 
     km_in = None
     if km is not None:
         km_in = km.reshape(B, H, 1, D).to(q.dtype).contiguous()
-    if perm is not None:
-        perm = perm.to(torch.int64).contiguous()
+    perm = _perm("prep_qk_int8", perm, B, H, Sk)
     lib = N.load()
     wsb = lib.vc_prep_qk_workspace_bytes(B, H, Sk, D)
     ws = _workspace(wsb, dev)
@@ -98,8 +109,7 @@ def prep_v_channel(v: torch.Tensor, *, perm: torch.Tensor | None = None):
     npad = (S + 127) // 128 * 128
     v8 = torch.empty((B, H, D, npad), dtype=torch.uint8, device=v.device)
     vs = torch.empty((B, H, D), dtype=torch.float32, device=v.device)
-    if perm is not None:
-        perm = perm.to(torch.int64).contiguous()
+    perm = _perm("prep_v_channel", perm, B, H, S)
     lib = N.load()
     ws = _workspace(lib.vc_prep_v_channel_workspace_bytes(B, H, S, D), v.device)
     with torch.cuda.device(v.device):
@@ -121,8 +131,7 @@ def prep_v_blocks(v: torch.Tensor, *, perm: torch.Tensor | None = None, channel_
     v8 = torch.empty((B, H, D, tiles * 128), dtype=torch.uint8, device=v.device)
     vs = torch.empty((B, H, D) if channel_scale else (B, H, tiles, D), dtype=torch.float32, device=v.device)
     means = torch.empty((B, H, tiles, D), dtype=torch.float16, device=v.device)
-    if perm is not None:
-        perm = perm.to(torch.int64).contiguous()
+    perm = _perm("prep_v_blocks", perm, B, H, S)
     lib = N.load()
     ws = _workspace(lib.vc_prep_v_blocks_workspace_bytes(B, H, S, D), v.device)
     with torch.cuda.device(v.device):

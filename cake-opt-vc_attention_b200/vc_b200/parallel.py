@@ -77,38 +77,46 @@ def sharded_attention(q, k, v, s: Shard, *, expcast=True, v_smooth=False, cluste
                              out=out, unit_range=s.local_units)
 
 
+def unit_rows(u: int, qtiles: int, Sq: int) -> int:
+    """First row of unit ``u`` in the flattened [B*H*Sq] row space."""
+    bh, qt = divmod(u, qtiles)
+    return bh * Sq + qt * 128
+
+
+def shard_rows(s: Shard, Sq: int) -> tuple[int, int]:
+    """The shard's rows [row_begin, row_end) in the flattened [B*H*Sq] row
+    space.  Consecutive units cover consecutive rows (a head's last tile is
+    ragged, the next head starts right after it), so this range is
+    contiguous."""
+    if s.unit_end <= s.unit_begin:
+        r = unit_rows(s.unit_begin, s.qtiles, Sq) if s.qtiles else 0
+        return r, r
+    last = s.unit_end - 1
+    r1 = unit_rows(last, s.qtiles, Sq) + min(128, Sq - (last % s.qtiles) * 128)
+    return unit_rows(s.unit_begin, s.qtiles, Sq), r1
+
+
 def gather_rows(local: torch.Tensor, s: Shard, B: int, H: int, Sq: int, group=None) -> torch.Tensor:
     """Assemble the full [B,H,Sq,D] output from every rank's shard with one
-    ``all_gather_into_tensor`` of fixed-size row blocks (NCCL over NVLink on
-    GPUs; gloo on CPU in tests)."""
+    all-gather of equal-size row blocks (NCCL over NVLink on GPUs; gloo on
+    CPU in tests).  ``local`` is the shard's [1, bh_end-bh_begin, Sq, D]
+    output; only its own rows are read."""
     import torch.distributed as dist
     world = s.world
     D = local.shape[-1]
-    rows_per_unit = 128
-    # pack this rank's unit rows into a fixed-size buffer (max units per rank)
-    max_units = -(-B * H * s.qtiles // world)
-    buf = torch.zeros(max_units * rows_per_unit, D, dtype=local.dtype, device=local.device)
-    lb, le = s.local_units
-    flat = local.reshape(-1, D)                       # [nbh * Sq, D]
-    for i, u in enumerate(range(lb, le)):
-        bh, qt = divmod(u, s.qtiles)
-        r0 = qt * 128
-        r1 = min(Sq, r0 + 128)
-        buf[i * 128:i * 128 + (r1 - r0)] = flat[bh * Sq + r0: bh * Sq + r1]
-    allbuf = torch.empty(world * buf.shape[0], D, dtype=local.dtype, device=local.device)
-    if hasattr(dist, "all_gather_into_tensor") and local.device.type == "cuda":
+    spans = [shard_rows(shard(B, H, Sq, world, r), Sq) for r in range(world)]
+    cap = max(e - b for b, e in spans)
+    rb, re = spans[s.rank]
+    off = s.bh_begin * Sq
+    flat = local.reshape(-1, D)
+    buf = torch.zeros(cap, D, dtype=local.dtype, device=local.device)
+    buf[:re - rb] = flat[rb - off:re - off]
+    allbuf = torch.empty(world * cap, D, dtype=local.dtype, device=local.device)
+    if local.device.type == "cuda":
         dist.all_gather_into_tensor(allbuf, buf, group=group)
     else:
-        parts = list(allbuf.chunk(world))
-        dist.all_gather(parts, buf, group=group)
-        allbuf = torch.cat(parts)
+        dist.all_gather(list(allbuf.chunk(world)), buf, group=group)
     out = torch.empty(B * H * Sq, D, dtype=local.dtype, device=local.device)
-    for r in range(world):
-        sr = shard(B, H, Sq, world, r)
-        blk = allbuf[r * buf.shape[0]:(r + 1) * buf.shape[0]]
-        for i, u in enumerate(range(sr.unit_begin, sr.unit_end)):
-            bh, qt = divmod(u, sr.qtiles)
-            r0 = qt * 128
-            r1 = min(Sq, r0 + 128)
-            out[bh * Sq + r0: bh * Sq + r1] = blk[i * 128:i * 128 + (r1 - r0)]
+    for r, (b, e) in enumerate(spans):
+        out[b:e] = allbuf[r * cap:r * cap + (e - b)]
     return out.reshape(B, H, Sq, D)

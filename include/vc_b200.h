@@ -52,7 +52,10 @@ const char* vc_last_error(void);
 
 /* Device error word (timeouts / invariant violations inside kernels).
  * Synchronous diagnostic call: copies the word of ``device`` into *code and
- * optionally clears it.
+ * optionally clears it.  Bits: 0x01-0x10 a bounded wait gave up (TMA, MMA,
+ * softmax, correction, producer), 0x20 tensor-memory allocation, 0x40 a bad
+ * kernel argument, 0x80 a permutation entry outside [0, S) (that row was read
+ * as zeros).
  * Replaces: no reference counterpart (the reference spins without bound,
  * third_party/sageattention_local/csrc/vc/vc_sm90.cu:114-128). */
 int vc_error_read(int device, uint32_t* code, int clear);

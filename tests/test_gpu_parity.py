@@ -83,6 +83,26 @@ def test_qk_int8_with_device_mean_and_permutation(ops, dtype):
     assert np.array_equal(_np(k8), e_k8) and np.array_equal(_np(ks), e_ks)
 
 
+def test_out_of_range_permutation_is_reported(ops):
+    """Permutation entries outside [0, S) are never dereferenced: those rows read
+    as zeros and the error word carries the bad-index bit (0x80).  A permutation
+    of the wrong shape is rejected on the host."""
+    v = torch.randn(1, 2, 300, 128).to(torch.bfloat16).cuda()
+    perm = torch.arange(300).repeat(1, 2, 1)
+    perm[0, 1, 5] = 300                       # one past the end
+    perm[0, 0, 7] = -1
+    perm = perm.cuda()
+    assert ops.error_word(0, clear=True) == 0
+    ops.prep_v_channel(v, perm=perm)
+    ops.prep_v_blocks(v, perm=perm)
+    ops.prep_qk_int8(v, v, perm=perm)
+    torch.cuda.synchronize()
+    assert ops.error_word(0, clear=True) == 0x80
+    for bad in (perm[0, 0], perm.float(), perm[:, :, :299]):
+        with pytest.raises(ValueError, match="perm must be"):
+            ops.prep_v_channel(v, perm=bad)
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("dim", [64, 128])
 @pytest.mark.parametrize("n", [1, 127, 128, 129, 1000])
