@@ -57,9 +57,11 @@ struct Params {
   int64_t osb, osh, oss;
   int64_t nqs, nks, ktiles, qtiles;
   int64_t unit_begin, unit_end;   // units (b*H+h)*qtiles + q_tile to compute
-  int64_t pair_begin;             // paired kernel: first (head, Q-tile pair) index
   float sm_scale;
   int exact_expcast;   // 1: unfused RN(RN(raw*f)-m) encoder instead of the folded affine one
+  // 2^8, 2^16, 2^24 as launch arguments: the byte packing multiplies by them
+  // (integer multiply-add on the FMA pipe) instead of shifting on the ALU pipe
+  uint32_t mul8, mul16, mul24;
 };
 
 struct __align__(8) Barriers {
@@ -437,8 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-#include "attention_fast.cuh"
-#include "attention_pair.cuh"
+#include "attention_softmax.cuh"
 #include "attention_alt.cuh"
 
 // ---------------------------------------------------------------------------
@@ -483,44 +484,17 @@ int launch_attn(const AttnArgs& a, const CUtensorMap& mk, const CUtensorMap& mv,
   return cudaGetLastError() == cudaSuccess ? VC_OK : VC_ERR_LAUNCH;
 }
 
-// VC_B200_KERNEL selects the kernel for ExpCast + channel-scaled V:
-// "alt" (default: alternating-tile softmax groups), "pair" (two Q tiles per
-// CTA), "split" (split-row softmax) or "general" (register accumulation).
-int kernel_choice() {
+// VC_B200_KERNEL=general selects the general kernel (register accumulation)
+// for ExpCast + channel-scaled V as well; the default there is the
+// alternating-tile kernel.
+bool use_general_kernel() {
   const char* e = getenv("VC_B200_KERNEL");
-  if (!e) return 3;
-  if (strcmp(e, "general") == 0) return 2;
-  if (strcmp(e, "split") == 0) return 1;
-  if (strcmp(e, "pair") == 0) return 0;
-  return 3;
+  return e && strcmp(e, "general") == 0;
 }
 
 struct Maps {
-  CUtensorMap q, k, v;
+  CUtensorMap k, v;
 };
-
-template <int D, typename OutT>
-int launch_fast(const Maps& m, const Params& p, int64_t units, cudaStream_t st) {
-  auto k = vc_attention_fast_kernel<D, OutT>;
-  const int smem = FastSmem<D>::kAlloc;
-  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return VC_ERR_LAUNCH;
-  k<<<static_cast<unsigned>(units), kFastThreads, smem, st>>>(m.k, m.v, p);
-  return cudaGetLastError() == cudaSuccess ? VC_OK : VC_ERR_LAUNCH;
-}
-
-template <int D, typename OutT>
-int launch_pair(const Maps& m, Params p, cudaStream_t st) {
-  auto k = vc_attention_pair_kernel<D, OutT>;
-  const int smem = PairSmem<D>::kAlloc;
-  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return VC_ERR_LAUNCH;
-  const int64_t pairs = (p.qtiles + 1) / 2;
-  const int64_t ub = p.unit_begin, ue = p.unit_end;
-  const int64_t h0 = ub / p.qtiles, h1 = (ue - 1) / p.qtiles;
-  p.pair_begin = h0 * pairs + (ub % p.qtiles) / 2;
-  const int64_t pair_end = h1 * pairs + ((ue - 1) % p.qtiles) / 2 + 1;
-  k<<<static_cast<unsigned>(pair_end - p.pair_begin), kPairThreads, smem, st>>>(m.q, m.k, m.v, p);
-  return cudaGetLastError() == cudaSuccess ? VC_OK : VC_ERR_LAUNCH;
-}
 
 template <int D, typename OutT>
 int launch_alt(const Maps& m, const Params& p, int64_t units, cudaStream_t st) {
@@ -533,10 +507,7 @@ int launch_alt(const Maps& m, const Params& p, int64_t units, cudaStream_t st) {
 
 template <int D, typename OutT>
 int dispatch_flags(const AttnArgs& a, const Maps& m, const Params& p, int64_t units, cudaStream_t st) {
-  const int choice = kernel_choice();
-  if (a.expcast && !a.block_values && choice == 3) return launch_alt<D, OutT>(m, p, units, st);
-  if (a.expcast && !a.block_values && choice == 0) return launch_pair<D, OutT>(m, p, st);
-  if (a.expcast && !a.block_values && choice == 1) return launch_fast<D, OutT>(m, p, units, st);
+  if (a.expcast && !a.block_values && !use_general_kernel()) return launch_alt<D, OutT>(m, p, units, st);
   const CUtensorMap& mk = m.k;
   const CUtensorMap& mv = m.v;
   if (a.expcast) {
@@ -564,7 +535,7 @@ int attention_fwd(const AttnArgs& a, cudaStream_t st) {
   if (ue == ub) return VC_OK;
   Maps m;
   const CUtensorMapSwizzle swk = a.D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  if (!make_map_3d(&m.q, a.q8, a.D, a.Sq, BH, a.D, 128, swk) || !make_map_3d(&m.k, a.k8, a.D, a.Sk, BH, a.D, 128, swk) ||
+  if (!make_map_3d(&m.k, a.k8, a.D, a.Sk, BH, a.D, 128, swk) ||
       !make_map_3d(&m.v, a.v8, ktiles * 128, a.D, BH, 128, a.D, CU_TENSOR_MAP_SWIZZLE_128B)) {
     set_last_error("vc_attention_fwd: cuTensorMapEncodeTiled failed");
     return VC_ERR_LAUNCH;
@@ -588,9 +559,11 @@ int attention_fwd(const AttnArgs& a, cudaStream_t st) {
   p.qtiles = qtiles;
   p.unit_begin = ub;
   p.unit_end = ue;
-  p.pair_begin = 0;
   p.sm_scale = a.sm_scale;
   p.exact_expcast = a.expcast == 2 ? 1 : 0;
+  p.mul8 = 1u << 8;
+  p.mul16 = 1u << 16;
+  p.mul24 = 1u << 24;
   const int64_t units = ue - ub;
   if (a.out_dtype == VC_DTYPE_BF16)
     return a.D == 128 ? dispatch_flags<128, __nv_bfloat16>(a, m, p, units, st)

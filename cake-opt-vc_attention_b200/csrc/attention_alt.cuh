@@ -1,6 +1,6 @@
 // Alternating-tile fused attention kernel (ExpCast, channel-scaled V, no
 // block means): the default kernel for that mode.  Included by attention.cu
-// after attention_fast.cuh and attention_pair.cuh (shares their helpers).
+// after attention_softmax.cuh (register-level helpers).
 //
 // One CTA owns one 128-row Q tile of a (batch, head).  Warp roles (384 thr):
 //   warps 0-3   softmax group 0: K tiles j = 0, 2, 4, ...
@@ -8,14 +8,20 @@
 //               thread t owns row t (TMEM lane t) of its tile and the whole
 //               128-key row; the only cross-group dependency is the running
 //               row maximum m_{j-1}, handed over through shared memory with
-//               an mbarrier per tile parity
+//               an mbarrier per tile parity and per warp (a warp needs only
+//               its own 32 rows, so no warp waits for another warp's skew)
 //   warp 8      K producer (TMA, 4-deep ring);  warp 10  V producer (3-deep)
 //   warp 9      TMEM allocator + QK^T issuer: QK(j) is issued as soon as K(j)
 //               has landed and the scores of tile j-2 have been read
 //   warp 11     P.V issuer: PV(j) as soon as P(j) and V(j) are ready
 //
 // Tensor memory (496 of 512 columns):
-//   S0 [0,128) S1 [128,256)   s32 scores of tiles j%2
+//   S0 [0,128) S1 [128,256)   s32 scores of tiles j%2.  Each buffer is preset
+//                             to 0x4B400000 (the bits of 1.5*2^23) and QK^T
+//                             accumulates onto it, so the scores arrive as
+//                             the bit patterns of 1.5*2^23 + s: floats
+//                             without an int->float conversion.  The softmax
+//                             group re-presets a buffer right after reading it.
 //   O  [256,256+D+16)         FP32 accumulator for the whole K loop; column D
 //                             accumulates P.1 (the ExpCast denominator) via a
 //                             row of E4M3 1.0 appended to every V tile
@@ -23,16 +29,35 @@
 //   Q  [480,480+D/4)          int8 Q tile (A operand of Q.K^T)
 // A group whose rows' maximum grew at tile j scales its lanes of O (and the
 // denominator column) after PV(j-1) completes and before it releases P(j).
+//
+// Barrier phases.  Every parity wait below is unconditional (taken on every
+// tile), so a waiter can never be two phases behind its barrier, and no
+// barrier can run ahead of its waiter (each next phase needs the waiter's own
+// next release).  In particular the group at tile j always waits pv_done[j&1]
+// for PV(j-1): that both frees P[j&1] (PV(j-2) precedes PV(j-1)) and orders
+// the O rescale after PV(j-1).  A conditional wait on a barrier that advances
+// every tile would alias phases and let the rescale race an MMA.
 #pragma once
 
 constexpr int kAltThreads = 384;
 constexpr int kKS = 4;   // K ring depth
 constexpr int kVS = 3;   // V ring depth
 constexpr uint32_t kAColS0 = 0, kAColS1 = 128, kAColO = 256, kAColP0 = 400, kAColP1 = 432, kAColQ = 480;
+// Magic addends that leave the ExpCast code (0..128) in the low byte of a
+// float's bits (ulp 1/128 on [2^16, 2^17)).  Byte k of a P word comes from
+// element k; with these addends the weighted sum
+//   bits(e0 + kMagFirst) + 2^8 bits(e1 + kMagRest) + 2^16 bits(e2 + kMagRest)
+//                        + 2^24 bits(e3 + kMagRest)         (mod 2^32)
+// is exactly the packed code word, because
+//   0x47C80000 + 0x47803800 * 0x01010100 == 0 (mod 2^32).
+constexpr float kMagFirst = 102400.0f;   // bits 0x47C80000
+constexpr float kMagRest = 65648.0f;     // bits 0x47803800
 
 struct __align__(8) AltBarriers {
   uint64_t k_full[kKS], k_empty[kKS], v_full[kVS], v_empty[kVS];
-  uint64_t q_ready, s_full[2], s_free[2], p_full[2], p_free[2], m_ready[2], o_done, o_final;
+  uint64_t q_ready, s_full[2], s_free[2], p_full[2], o_final;
+  uint64_t pv_done[2];      // PV(i) completes pv_done[(i+1)&1]: the group of tile i+1 waits on it
+  uint64_t m_ready[2][4];   // [tile parity][warp of the group]
 };
 
 template <int D>
@@ -79,10 +104,9 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       mbar_init(&bar->s_full[b], 1);
       mbar_init(&bar->s_free[b], 128);
       mbar_init(&bar->p_full[b], 128);
-      mbar_init(&bar->p_free[b], 1);
-      mbar_init(&bar->m_ready[b], 128);
+      mbar_init(&bar->pv_done[b], 1);
+      for (int q = 0; q < 4; ++q) mbar_init(&bar->m_ready[b][q], 32);
     }
-    mbar_init(&bar->o_done, 1);
     mbar_init(&bar->o_final, 1);
     fence_barrier_init();
   }
@@ -132,13 +156,14 @@ __global__ void __launch_bounds__(kAltThreads, 1)
         for (int j = 0; j < T; ++j) {
           const int s = j % kKS, b = j & 1;
           if (!mbar_wait(&bar->k_full[s], (j / kKS) & 1, kErrTimeoutMma)) break;
-          if (j >= 2 && !mbar_wait(&bar->s_free[b], ((j - 2) >> 1) & 1, kErrTimeoutMma)) break;
+          // completion (j>>1) of s_free[b]: the preset after tile j-2 was read (or the initial one)
+          if (!mbar_wait(&bar->s_free[b], (j >> 1) & 1, kErrTimeoutMma)) break;
           tc_fence_after();
           const uint64_t kd = kdesc0 + s * kStepK;
           const uint32_t scol = tmem + (b ? kAColS1 : kAColS0);
 #pragma unroll
           for (int kk = 0; kk < D / 32; ++kk)
-            mma_i8_ts(scol, tmem + kAColQ + kk * 8, kd + 2 * kk, idesc_qk, kk > 0);
+            mma_i8_ts(scol, tmem + kAColQ + kk * 8, kd + 2 * kk, idesc_qk, 1u);   // onto the preset
           mma_commit(&bar->k_empty[s]);
           mma_commit(&bar->s_full[b]);
         }
@@ -163,8 +188,7 @@ __global__ void __launch_bounds__(kAltThreads, 1)
         for (int kk = 0; kk < 4; ++kk)
           mma_f8_ts(tmem + kAColO, pcol + kk * 8, vd + 2 * kk, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&bar->v_empty[s]);
-        mma_commit(&bar->p_free[b]);
-        mma_commit(&bar->o_done);
+        mma_commit(&bar->pv_done[(j + 1) & 1]);
       }
       if (ok) mma_commit(&bar->o_final);
     }
@@ -193,7 +217,18 @@ __global__ void __launch_bounds__(kAltThreads, 1)
     }
     const float qscale = row_valid ? p.qs[bh * p.nqs + (row >> 4) * 8 + (row & 7)] : 0.f;
     const float scale = p.sm_scale;
-    const uint64_t bias2 = pk2f(kBias, kBias), mag2 = pk2f(kMag, kMag);
+    const uint64_t bias2 = pk2f(kBias, kBias);
+    const uint64_t magA = pk2f(kMagFirst, kMagRest), magB = pk2f(kMagRest, kMagRest);
+    const uint32_t mul8 = p.mul8, mul16 = p.mul16, mul24 = p.mul24;
+    {
+      // preset this group's score buffer S[w] for its first tile
+      const uint32_t scol = tmem + lane_base + (w ? kAColS1 : kAColS0);
+#pragma unroll
+      for (int c = 0; c < 128; c += 32) tmem_fill32(scol + c, kBiasBits);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bar->s_free[w]);
+    }
     bool ok = true;
     float4 ksv_next = w < T ? __ldg(reinterpret_cast<const float4*>(p.ks + bh * p.nks + w * 4)) : make_float4(1, 1, 1, 1);
     for (int j = w; j < T; j += 2) {
@@ -210,10 +245,9 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       tmem_ld32(scol + 64, *reinterpret_cast<uint32_t(*)[32]>(raw + 64));
       tmem_ld32(scol + 96, *reinterpret_cast<uint32_t(*)[32]>(raw + 96));
       tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&bar->s_free[b]);   // QK(j+2) may now overwrite this S buffer
+      // preset S[b] again for QK(j+2); released once the stores have landed (below)
 #pragma unroll
-      for (int c = 0; c < 128; ++c) raw[c] += kBiasBits;
+      for (int c = 0; c < 128; c += 32) tmem_fill32(scol + c, kBiasBits);
       if (j == T - 1) {
         const int valid = static_cast<int>(p.Sk - int64_t(j) * 128);
 #pragma unroll
@@ -234,17 +268,20 @@ __global__ void __launch_bounds__(kAltThreads, 1)
           mx = max3f(mx, __uint_as_float(raw[8 * k + 2 * g]), __uint_as_float(raw[8 * k + 2 * g + 1]));
         if (mx > 0.f) lmax = fmaxf(lmax, __fmul_rn(__fsub_rn(mx, kBias), f1[g]));
       }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bar->s_free[b]);   // QK(j+2) may now accumulate onto the preset
       // running maximum handed over from the other group's previous tile
       float mprev = -5000000.0f;
       if (j >= 1) {
-        ok = mbar_wait_warp(&bar->m_ready[b ^ 1], ((j - 1) >> 1) & 1, kErrTimeoutSoftmax);
+        ok = mbar_wait_warp(&bar->m_ready[b ^ 1][quarter], ((j - 1) >> 1) & 1, kErrTimeoutSoftmax);
         if (!ok) break;
         mprev = mbuf[(b ^ 1) * 128 + t];
       }
       const float mn = fmaxf(mprev, lmax);
       const float alpha = expf(mprev - mn);
       mbuf[b * 128 + t] = mn;
-      mbar_arrive(&bar->m_ready[b]);
+      mbar_arrive(&bar->m_ready[b][quarter]);
       uint32_t pw[32];
       float gain[4];
 #pragma unroll
@@ -255,7 +292,7 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       if (__all_sync(0xffffffffu, safe)) {
 #pragma unroll
         for (int wd = 0; wd < 32; ++wd) {
-          uint32_t hw[2];
+          uint32_t fw[4];
 #pragma unroll
           for (int q2 = 0; q2 < 2; ++q2) {
             const int c = 4 * wd + 2 * q2;
@@ -264,17 +301,15 @@ __global__ void __launch_bounds__(kAltThreads, 1)
             up2(f2_sub(pk2(raw[c], raw[c + 1]), bias2), a, bb);
             const float va = fma_sat(__uint_as_float(a), gain[g], cb);
             const float vb = fma_sat(__uint_as_float(bb), gain[g], cb);
-            uint32_t wa, wb;
-            up2(f2_add(pk2f(va, vb), mag2), wa, wb);
-            hw[q2] = __byte_perm(wa, wb, 0x0040);
+            up2(f2_add(pk2f(va, vb), q2 ? magB : magA), fw[2 * q2], fw[2 * q2 + 1]);
           }
-          pw[wd] = __byte_perm(hw[0], hw[1], 0x5410);
+          pw[wd] = fw[0] + fw[1] * mul8 + fw[2] * mul16 + fw[3] * mul24;
         }
       } else {
         const uint64_t m2 = pk2f(mn, mn);
 #pragma unroll
         for (int wd = 0; wd < 32; ++wd) {
-          uint32_t hw[2];
+          uint32_t fw[4];
 #pragma unroll
           for (int q2 = 0; q2 < 2; ++q2) {
             const int c = 4 * wd + 2 * q2;
@@ -284,23 +319,18 @@ __global__ void __launch_bounds__(kAltThreads, 1)
             up2(sh, a, bb);
             const float va = fma_sat(__uint_as_float(a), kExpA128, kExpB128);
             const float vb = fma_sat(__uint_as_float(bb), kExpA128, kExpB128);
-            uint32_t wa, wb;
-            up2(f2_add(pk2f(va, vb), mag2), wa, wb);
-            hw[q2] = __byte_perm(wa, wb, 0x0040);
+            up2(f2_add(pk2f(va, vb), q2 ? magB : magA), fw[2 * q2], fw[2 * q2 + 1]);
           }
-          pw[wd] = __byte_perm(hw[0], hw[1], 0x5410);
+          pw[wd] = fw[0] + fw[1] * mul8 + fw[2] * mul16 + fw[3] * mul24;
         }
       }
-      // PV(j-2) must be complete before P(j) reuses its buffer -- and before a
-      // parity wait on o_done for PV(j-1) (o_done then lags by at most one phase)
-      if (j >= 2) {
-        ok = mbar_wait_warp(&bar->p_free[b], ((j - 2) >> 1) & 1, kErrTimeoutSoftmax);
+      // PV(j-1) complete (hence PV(j-2) too): P[b] is free and O may be rescaled
+      if (j >= 1) {
+        ok = mbar_wait_warp(&bar->pv_done[b], ((j - 1) >> 1) & 1, kErrTimeoutSoftmax);
         if (!ok) break;
       }
       // rescale O (and the denominator column) between PV(j-1) and PV(j) if any max grew
       if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
-        ok = mbar_wait_warp(&bar->o_done, (j - 1) & 1, kErrTimeoutSoftmax);
-        if (!ok) break;
         tc_fence_after();
         const uint32_t ocol = tmem + lane_base + kAColO;
 #pragma unroll

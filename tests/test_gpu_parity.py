@@ -279,17 +279,28 @@ def test_fast_and_general_kernels_agree_with_oracle(ops, monkeypatch, shape):
     exact = ops.attention_fwd(*args, out_dtype=torch.float32, expcast="exact")
     monkeypatch.setenv("VC_B200_KERNEL", "general")
     general = ops.attention_fwd(*args, out_dtype=torch.float32)
-    monkeypatch.setenv("VC_B200_KERNEL", "split")
-    split = ops.attention_fwd(*args, out_dtype=torch.float32)
-    monkeypatch.setenv("VC_B200_KERNEL", "pair")
-    pair = ops.attention_fwd(*args, out_dtype=torch.float32)
     monkeypatch.delenv("VC_B200_KERNEL")
     ref = O.reference(_cpu_state(st))
-    for out in (fast, exact, general, split, pair):
+    for out in (fast, exact, general):
         m = O.metrics(out.cpu(), ref)
         assert m["cos"] >= COS_MIN and m["rel_l2"] <= REL_MAX, m
     # the exact encoder reproduces the oracle's bytes: only accumulation order differs
     assert O.metrics(exact.cpu(), ref)["rel_l2"] <= 2e-5
+
+
+@pytest.mark.parametrize("sm_scale", [None, 1.0])
+def test_attention_is_bitwise_repeatable(ops, sm_scale):
+    """The pipelined kernel has no timing-dependent arithmetic: repeated calls
+    on the same payloads give identical bits (many K tiles, frequent maximum
+    changes with the larger scale)."""
+    shape = (1, 8, 8192, 128)
+    q, k, v = qk_inputs(33, shape, torch.bfloat16, 3 ** 0.5)
+    st = _device_state(ops, q, k, v)
+    args = (st["q"], st["qs"], st["k"], st["ks"], st["v"], st["vs"], None)
+    kw = {} if sm_scale is None else {"sm_scale": sm_scale}
+    first = ops.attention_fwd(*args, **kw)
+    for _ in range(6):
+        assert torch.equal(ops.attention_fwd(*args, **kw), first)
 
 
 def test_attention_large_logits_and_rescales(ops):
