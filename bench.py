@@ -308,12 +308,12 @@ def main():
     hbm, bf16, bf16_sus, basis = peaks()
     peak_tops = 2.0 * bf16          # dense INT8/FP8 tensor rate is 2x the measured dense BF16 rate
     achieved = ops_launch / (att_ms * 1e-3) / 1e12
-    # DRAM bytes per launch: dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of the
-    # alternating-tile kernel on a 6-head slice of config 2 (116.4 MB), scaled by the heads in this
-    # launch (profiles/vc_attention_alt_kernel_1x6x37741.txt); D128, ExpCast, channel-scaled V only.
+    # DRAM bytes per launch: dram__bytes_read.sum + dram__bytes_write.sum of the alternating-tile
+    # kernel captured by ncu on the full config-2 launch (409.5 MB + 237.7 MB; profiles/
+    # launches_bench_c2.txt), scaled by the heads in this launch; D128, ExpCast, channel-scaled V.
     traffic = None
     if D == 128 and not smooth and S == 37741:
-        traffic = 116.44e6 / 6 * nbh
+        traffic = 647.2e6 / 28 * nbh
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_tops, "unit": "TFLOP/s",
                 "frac": achieved / peak_tops, "traffic": traffic,
                 "kernel": "vc_attention_alt_kernel", "peak_basis": f"2 x bf16_tflops ({basis}, MEASURED_PEAKS.json)",

@@ -217,6 +217,50 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, uint64_
       : "memory");
 }
 
+// Untiled bulk copy global -> shared (CTA-local, no multicast); both addresses
+// 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// N values of type T (16-byte aligned, N*sizeof(T) a multiple of 8) from
+// shared memory, widened to FP32.
+template <typename T, int N>
+__device__ __forceinline__ void load_vec_smem(const T* p, float (&out)[N]) {
+  static_assert((N * sizeof(T)) % 8 == 0, "8/16/32-byte vectors");
+  constexpr int kWords = N * sizeof(T) / 4;
+  uint32_t w[kWords];
+  const uint32_t a = smem_u32(p);
+  if constexpr (kWords % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < kWords / 4; ++i)
+      asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(w[4 * i]), "=r"(w[4 * i + 1]), "=r"(w[4 * i + 2]), "=r"(w[4 * i + 3])
+                   : "r"(a + 16 * i));
+  } else {
+#pragma unroll
+    for (int i = 0; i < kWords / 2; ++i)
+      asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(w[2 * i]), "=r"(w[2 * i + 1]) : "r"(a + 8 * i));
+  }
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) out[i] = __uint_as_float(w[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i) {
+      T lo, hi;
+      uint16_t l16 = static_cast<uint16_t>(w[i] & 0xFFFFu), h16 = static_cast<uint16_t>(w[i] >> 16);
+      memcpy(&lo, &l16, 2);
+      memcpy(&hi, &h16, 2);
+      out[2 * i] = to_f32(lo);
+      out[2 * i + 1] = to_f32(hi);
+    }
+  }
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }

@@ -82,11 +82,30 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// One Sage INT8 value: q = x/scale, q += 0.5*sign(q), truncate.
-__device__ __forceinline__ int8_t sage_i8(float x, float scale) {
-  float q = __fdiv_rn(x, scale);
-  q = __fadd_rn(q, q >= 0.f ? 0.5f : -0.5f);
-  return static_cast<int8_t>(__float2int_rz(q));
+// One Sage INT8 value: q = RN(x/scale), q += 0.5*sign(q), truncate toward 0.
+// Done without conversion-unit instructions (the quantiser is otherwise
+// bound by them):
+//  * RN(x/scale) by Markstein's correction step (Handbook of Floating-Point
+//    Arithmetic, Muller et al., 2nd ed., sec. 4.7): with y = RN(1/scale)
+//    (rscale, correctly rounded, computed once per scale group) and
+//    q0 = RN(x*y) within one ulp of x/scale, the remainder
+//    r = fma(-q0, scale, x) is exact and RN(q0 + r*y) = RN(x/scale).
+//    Tiny quotients (|q| < 0.5) give 0 whatever their last bits.
+//  * trunc(RN(q + 0.5*sign q)) equals round-half-away-from-zero of q (the
+//    addition can only round when it crosses a power of two, which does not
+//    move the integer part): RNE via the 1.5*2^23 magic add, then ties
+//    (|q - RNE(q)| == 1/2) moved away from zero.  |q| <= 127.5 here.
+__device__ __forceinline__ int8_t sage_i8(float x, float scale, float rscale) {
+  const float q0 = __fmul_rn(x, rscale);
+  const float r = __fmaf_rn(-q0, scale, x);
+  const float q = __fmaf_rn(r, rscale, q0);
+  const float big = __fadd_rn(q, 12582912.f);
+  const float rne = __fsub_rn(big, 12582912.f);
+  const float d = __fsub_rn(q, rne);
+  int i = static_cast<int>(__float_as_uint(big) - 0x4B400000u);
+  if (d == 0.5f && q > 0.f) ++i;
+  if (d == -0.5f && q < 0.f) --i;
+  return static_cast<int8_t>(i);
 }
 
 template <int N>
@@ -105,95 +124,196 @@ __device__ __forceinline__ void store_i8(int8_t* p, const int8_t (&v)[N]) {
   }
 }
 
-// Q: one warp per 16-row block; group g in 0..7 holds rows g and g+8.
-// Lanes 0-15 read row g, lanes 16-31 row g+8, D/16 channels each.
-template <typename T, int D>
-__global__ void __launch_bounds__(256) quant_q(const T* __restrict__ q, int64_t H, int64_t S, int64_t sb, int64_t sh,
-                                               int64_t ss, int8_t* __restrict__ q8, float* __restrict__ qs,
-                                               int64_t nblk16) {
-  constexpr int E = D / 16;
-  const int lane = threadIdx.x & 31;
-  const int64_t blk = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  const int64_t bh = blockIdx.y;
-  if (blk >= nblk16) return;
-  const int col = (lane & 15) * E;
-  const int half = lane >> 4;
-  const int64_t nscale = nblk16 * 8;
-#pragma unroll 2
-  for (int g = 0; g < 8; ++g) {
-    const int64_t row = blk * 16 + g + half * 8;
-    float x[E];
-    if (row < S) {
-      load_vec<T, E>(row_ptr(q, bh, H, sb, sh, ss, row) + col, x);
-    } else {
-#pragma unroll
-      for (int i = 0; i < E; ++i) x[i] = 0.f;
-    }
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < E; ++i) amax = fmaxf(amax, fabsf(x[i]));
-    amax = warp_max(amax);
-    const float scale = __fadd_rn(__fdiv_rn(amax, 127.f), 1e-7f);
-    int8_t o[E];
-#pragma unroll
-    for (int i = 0; i < E; ++i) o[i] = sage_i8(x[i], scale);
-    if (row < S) store_i8<E>(q8 + (bh * S + row) * D + col, o);
-    if (lane == 0) qs[bh * nscale + blk * 8 + g] = scale;
-  }
-}
+// ---------------------------------------------------------------------------
+// Q and K quantisation tiles, one persistent kernel.
+//
+// A tile is 128 tokens of one (b,h): Q tiles first, then K tiles.  A producer
+// warp streams each tile into a shared-memory ring with untiled bulk copies:
+// one copy per tile when its rows are contiguous, else one per row (arbitrary
+// row strides and the K permutation gather).  Two groups of eight compute
+// warps take alternate tiles, quantise from shared memory and write int8 rows
+// and scales with coalesced stores.
+//   Q tile: warp w owns the 16-row Sage block w; scale group g = rows g, g+8.
+//   K tile: scale group tld = rows 8i + 2 tld + {0,1}; warps w and w+4 split
+//           the 16 i values of group tld = w & 3 and combine their maxima
+//           through shared memory (one named barrier per tile).
+// ---------------------------------------------------------------------------
+constexpr int kTileWarps = 8;                              // per compute group
+constexpr int kTileGroups = 2;
+constexpr int kTileThreads = (kTileGroups * kTileWarps + 1) * 32;   // + producer warp
 
-// K: one warp per (128-row block, tld); its 32 rows are blk*128 + 8i + 2tld + {0,1}.
 template <typename T, int D>
-__global__ void __launch_bounds__(128) quant_k(const T* __restrict__ k, int64_t H, int64_t S, int64_t sb, int64_t sh,
-                                               int64_t ss, const int64_t* __restrict__ perm,
-                                               const T* __restrict__ km, int8_t* __restrict__ k8,
-                                               float* __restrict__ ks, int64_t nblk) {
+struct TileRing {
+  static constexpr int kRow = D * int(sizeof(T));
+  static constexpr int kStage = 128 * kRow;
+  static constexpr int kStages = (196608 / kStage) < 4 ? (196608 / kStage) : 4;
+  static constexpr int kOffBar = kStages * kStage;
+  static constexpr int kOffRed = kOffBar + 2 * kStages * 8;
+  static constexpr int kBytes = kOffRed + kTileGroups * 2 * kTileWarps * 4;
+  static_assert(kStages >= 2, "two stages at least");
+};
+
+struct QKTileParams {
+  const void* q;
+  const void* k;
+  int64_t H, Sq, Sk;
+  int64_t qsb, qsh, qss, ksb, ksh, kss;
+  const int64_t* perm;
+  const void* km;
+  int8_t* q8;
+  float* qs;
+  int8_t* k8;
+  float* ks;
+  int64_t qtiles, ktiles, nq, total;   // tiles per head (Q, K); Q tile count; all tiles
+  int64_t nscale;                       // Q scales per head
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kTileThreads, 1) qk_tiles(QKTileParams p) {
+  using L = TileRing<T, D>;
   constexpr int E = D / 16;
-  const int lane = threadIdx.x & 31;
-  const int tld = threadIdx.x >> 5;  // 4 warps
-  const int64_t blk = blockIdx.x;
-  const int64_t bh = blockIdx.y;
-  const int col = (lane & 15) * E;
-  const int half = lane >> 4;
-  float kmv[E];
-#pragma unroll
-  for (int i = 0; i < E; ++i) kmv[i] = to_f32(km[bh * D + col + i]);
-  float x[16][E];
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int64_t row = blk * 128 + 8 * i + 2 * tld + half;
-    if (row < S) {
-      const int64_t src = perm ? perm[bh * S + row] : row;
-      float raw[E];
-      if (src >= 0 && src < S) {
-        load_vec<T, E>(row_ptr(k, bh, H, sb, sh, ss, src) + col, raw);
-      } else {
-        raise_error(kErrBadIndex);   // out-of-range permutation entry: the row reads as zeros
-#pragma unroll
-        for (int j = 0; j < E; ++j) raw[j] = 0.f;
+  extern __shared__ __align__(128) uint8_t sm[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + L::kOffBar);
+  uint64_t* empty = full + L::kStages;
+  const int gwarp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = gwarp / kTileWarps, warp = gwarp % kTileWarps;
+  float* red = reinterpret_cast<float*>(sm + L::kOffRed) + grp * 2 * kTileWarps;   // [K-tile parity][warp]
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < L::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kTileWarps * 32);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (gwarp == kTileGroups * kTileWarps) {
+    // ------------------------------------------------------------ producer
+    int n = 0;
+    for (int64_t t = blockIdx.x; t < p.total; t += gridDim.x, ++n) {
+      const int s = n % L::kStages;
+      if (n >= L::kStages && !mbar_wait(&empty[s], ((n / L::kStages) & 1) ^ 1, kErrTimeoutProducer)) break;
+      const bool isq = t < p.nq;
+      const int64_t tt = isq ? t : t - p.nq;
+      const int64_t tiles = isq ? p.qtiles : p.ktiles;
+      const int64_t bh = tt / tiles, r0 = (tt - bh * tiles) * 128;
+      const int64_t S = isq ? p.Sq : p.Sk;
+      const int rows = static_cast<int>(min64(128, S - r0));
+      const int64_t b = bh / p.H, h = bh - b * p.H;
+      const T* base = static_cast<const T*>(isq ? p.q : p.k) + b * (isq ? p.qsb : p.ksb) + h * (isq ? p.qsh : p.ksh);
+      const int64_t ss = isq ? p.qss : p.kss;
+      if (lane == 0) mbar_expect_tx(&full[s], static_cast<uint32_t>(rows * L::kRow));
+      __syncwarp();
+      uint8_t* dst = sm + s * L::kStage;
+      if (ss == D && (isq || !p.perm)) {   // contiguous rows: one copy for the tile
+        if (lane == 0) bulk_load(dst, base + r0 * ss, static_cast<uint32_t>(rows * L::kRow), &full[s]);
+        continue;
       }
+      for (int r = lane; r < rows; r += 32) {
+        int64_t src = r0 + r;
+        if (!isq && p.perm) {
+          src = p.perm[bh * S + src];
+          if (src < 0 || src >= S) {
+            raise_error(kErrBadIndex);   // out-of-range permutation entry: read row 0 instead
+            src = 0;
+          }
+        }
+        bulk_load(dst + r * L::kRow, base + src * ss, L::kRow, &full[s]);
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- compute
+  const int col = (lane & 15) * E;
+  const int hf = lane >> 4;
+  int n = grp, nk = 0;
+  for (int64_t t = blockIdx.x + int64_t(grp) * gridDim.x; t < p.total; t += kTileGroups * int64_t(gridDim.x), n += kTileGroups) {
+    const int s = n % L::kStages;
+    if (!mbar_wait_warp(&full[s], (n / L::kStages) & 1, kErrTimeoutProducer)) return;
+    const T* tile = reinterpret_cast<const T*>(sm + s * L::kStage);
+    const bool isq = t < p.nq;
+    const int64_t tt = isq ? t : t - p.nq;
+    const int64_t tiles = isq ? p.qtiles : p.ktiles;
+    const int64_t bh = tt / tiles, r0 = (tt - bh * tiles) * 128;
+    const int64_t S = isq ? p.Sq : p.Sk;
+    const int rows = static_cast<int>(min64(128, S - r0));
+    if (isq) {
+      // Sage Q block: rows 16w .. 16w+15 of the tile, scale groups g = rows {g, g+8}
+#pragma unroll 2
+      for (int g = 0; g < 8; ++g) {
+        const int r = 16 * warp + g + 8 * hf;
+        float x[E];
+        if (r < rows) {
+          load_vec_smem<T, E>(tile + r * D + col, x);
+        } else {
 #pragma unroll
-      for (int j = 0; j < E; ++j) {
-        x[i][j] = round_as(__fsub_rn(raw[j], kmv[j]), static_cast<T*>(nullptr));
-        amax = fmaxf(amax, fabsf(x[i][j]));
+          for (int i = 0; i < E; ++i) x[i] = 0.f;
+        }
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < E; ++i) amax = fmaxf(amax, fabsf(x[i]));
+        amax = warp_max(amax);
+        const float scale = __fadd_rn(__fdiv_rn(amax, 127.f), 1e-7f);
+        const float rscale = __frcp_rn(scale);
+        int8_t o[E];
+#pragma unroll
+        for (int i = 0; i < E; ++i) o[i] = sage_i8(x[i], scale, rscale);
+        if (r < rows) store_i8<E>(p.q8 + (bh * S + r0 + r) * D + col, o);
+        // scales exist for the 16-row blocks of Sq padded to 64 rows (all-padding blocks get 1e-7)
+        const int64_t blk16 = (r0 >> 4) + warp;
+        if (lane == 0 && blk16 * 8 < p.nscale) p.qs[bh * p.nscale + blk16 * 8 + g] = scale;
       }
     } else {
+      // K: centre as RN_T(k - km), then Sage per-thread groups of 32 rows
+      const int tld = warp & 3, ih = warp >> 2;
+      float kmv[E];
+      {
+        const T* kmp = static_cast<const T*>(p.km) + bh * D + col;
 #pragma unroll
-      for (int j = 0; j < E; ++j) x[i][j] = 0.f;
+        for (int i = 0; i < E; ++i) kmv[i] = to_f32(kmp[i]);
+      }
+      T x[8][E];   // centred values, exactly representable in T: keep them narrow
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int r = 8 * (8 * ih + i) + 2 * tld + hf;
+        if (r < rows) {
+          float raw[E];
+          load_vec_smem<T, E>(tile + r * D + col, raw);
+#pragma unroll
+          for (int j = 0; j < E; ++j) {
+            const float c = round_as(__fsub_rn(raw[j], kmv[j]), static_cast<T*>(nullptr));
+            x[i][j] = static_cast<T>(c);
+            amax = fmaxf(amax, fabsf(c));
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < E; ++j) x[i][j] = static_cast<T>(0.f);
+        }
+      }
+      amax = warp_max(amax);
+      // double-buffered by K-tile parity: every K tile has a barrier, so no warp
+      // rewrites a slot another warp may still be reading
+      float* rb = red + (nk & 1) * kTileWarps;
+      ++nk;
+      if (lane == 0) rb[warp] = amax;
+      asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "n"(kTileWarps * 32) : "memory");
+      amax = fmaxf(rb[tld], rb[tld + 4]);
+      const float scale = __fadd_rn(__fdiv_rn(amax, 127.f), 1e-7f);
+      const float rscale = __frcp_rn(scale);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int r = 8 * (8 * ih + i) + 2 * tld + hf;
+        int8_t o[E];
+#pragma unroll
+        for (int j = 0; j < E; ++j) o[j] = sage_i8(to_f32(x[i][j]), scale, rscale);
+        if (r < rows) store_i8<E>(p.k8 + (bh * S + r0 + r) * D + col, o);
+      }
+      if (lane == 0 && ih == 0) p.ks[bh * (p.ktiles * 4) + (r0 >> 7) * 4 + tld] = scale;
     }
+    mbar_arrive(&empty[s]);
   }
-  amax = warp_max(amax);
-  const float scale = __fadd_rn(__fdiv_rn(amax, 127.f), 1e-7f);
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int64_t row = blk * 128 + 8 * i + 2 * tld + half;
-    int8_t o[E];
-#pragma unroll
-    for (int j = 0; j < E; ++j) o[j] = sage_i8(x[i][j], scale);
-    if (row < S) store_i8<E>(k8 + (bh * S + row) * D + col, o);
-  }
-  if (lane == 0) ks[bh * (nblk * 4) + blk * 4 + tld] = scale;
 }
 
 template <typename T, int D>
@@ -214,12 +334,29 @@ int launch_prep_qk(const PrepQKArgs& a, cudaStream_t st) {
   } else if (a.km_out) {
     cudaMemcpyAsync(a.km_out, a.km_in, BH * D * sizeof(T), cudaMemcpyDeviceToDevice, st);
   }
-  const int64_t nblk16 = (a.Sq + 63) / 64 * 4;
-  quant_q<T, D><<<dim3((nblk16 + 7) / 8, BH), 256, 0, st>>>(static_cast<const T*>(a.q), a.H, a.Sq, a.qsb, a.qsh,
-                                                            a.qss, a.q8, a.qs, nblk16);
-  const int64_t nblk = (a.Sk + 127) / 128;
-  quant_k<T, D><<<dim3(nblk, BH), 128, 0, st>>>(static_cast<const T*>(a.k), a.H, a.Sk, a.ksb, a.ksh, a.kss, a.perm,
-                                                km, a.k8, a.ks, nblk);
+  QKTileParams tp;
+  tp.q = a.q;
+  tp.k = a.k;
+  tp.H = a.H;
+  tp.Sq = a.Sq;
+  tp.Sk = a.Sk;
+  tp.qsb = a.qsb; tp.qsh = a.qsh; tp.qss = a.qss;
+  tp.ksb = a.ksb; tp.ksh = a.ksh; tp.kss = a.kss;
+  tp.perm = a.perm;
+  tp.km = km;
+  tp.q8 = a.q8; tp.qs = a.qs; tp.k8 = a.k8; tp.ks = a.ks;
+  tp.qtiles = (a.Sq + 127) / 128;
+  tp.ktiles = (a.Sk + 127) / 128;
+  tp.nq = BH * tp.qtiles;
+  tp.total = tp.nq + BH * tp.ktiles;
+  tp.nscale = (a.Sq + 63) / 64 * 32;
+  auto kern = qk_tiles<T, D>;
+  constexpr int smem = TileRing<T, D>::kBytes;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return VC_ERR_LAUNCH;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t grid = min64(tp.total, static_cast<int64_t>(sms));
+  kern<<<static_cast<unsigned>(grid), kTileThreads, smem, st>>>(tp);
   return cudaGetLastError() == cudaSuccess ? VC_OK : VC_ERR_LAUNCH;
 }
 

@@ -83,6 +83,51 @@ def test_qk_int8_with_device_mean_and_permutation(ops, dtype):
     assert np.array_equal(_np(k8), e_k8) and np.array_equal(_np(ks), e_ks)
 
 
+def _tie_heavy(seed, shape):
+    """FP32 Q/K whose quotients x/scale land on (or next to) the .5 ties of the
+    Sage rounding: every 2-row Q scale group and every 32-row K scale group
+    holds one element 127*c (so scale = RN(RN(127c/127) + 1e-7)) and the rest
+    are RN((k + 1/2) * scale) for random integers k."""
+    g = np.random.default_rng(seed)
+    B, H, S, D = shape
+    f32 = np.float32
+
+    def fill(x, rows):
+        c = f32(g.uniform(0.01, 3.0))
+        amax = f32(f32(127.0) * c)
+        scale = f32(f32(amax / f32(127.0)) + f32(1e-7))
+        k = g.integers(-126, 126, size=(len(rows), D)).astype(f32)
+        x[rows] = ((k + f32(0.5)) * scale).astype(f32)
+        x[rows[0], g.integers(0, D)] = amax * (1 if g.random() < 0.5 else -1)
+
+    q = np.zeros(shape, f32)
+    k = np.zeros(shape, f32)
+    for b in range(B):
+        for h in range(H):
+            for blk in range(0, S, 16):
+                for gg in range(8):
+                    rows = [r for r in (blk + gg, blk + gg + 8) if r < S]
+                    if rows:
+                        fill(q[b, h], rows)
+            for blk in range(0, S, 128):
+                for tld in range(4):
+                    rows = [r for i in range(16) for r in (blk + 8 * i + 2 * tld, blk + 8 * i + 2 * tld + 1) if r < S]
+                    if rows:
+                        fill(k[b, h], rows)
+    return torch.from_numpy(q), torch.from_numpy(k)
+
+
+@pytest.mark.parametrize("shape", [(1, 2, 1000, 128), (1, 1, 300, 64)])
+def test_qk_int8_bit_exact_on_rounding_ties(ops, shape):
+    q, k = _tie_heavy(7, shape)
+    km = torch.zeros(shape[0], shape[1], 1, shape[3])
+    q8, qs, k8, ks, _ = ops.prep_qk_int8(q.cuda(), k.cuda(), km=km.cuda())
+    e_q8, e_qs, e_k8, e_ks = O.per_thread_int8(q, k, km)
+    assert np.array_equal(_np(qs), e_qs) and np.array_equal(_np(ks), e_ks)
+    assert np.array_equal(_np(q8), e_q8)
+    assert np.array_equal(_np(k8), e_k8)
+
+
 def test_out_of_range_permutation_is_reported(ops):
     """Permutation entries outside [0, S) are never dereferenced: those rows read
     as zeros and the error word carries the bad-index bit (0x80).  A permutation
