@@ -496,9 +496,9 @@ struct Maps {
   CUtensorMap k, v;
 };
 
-template <int D, typename OutT>
+template <int D, typename OutT, bool BV>
 int launch_alt(const Maps& m, const Params& p, int64_t units, cudaStream_t st) {
-  auto k = vc_attention_alt_kernel<D, OutT>;
+  auto k = vc_attention_alt_kernel<D, OutT, BV>;
   const int smem = AltSmem<D>::kAlloc;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return VC_ERR_LAUNCH;
   k<<<static_cast<unsigned>(units), kAltThreads, smem, st>>>(m.k, m.v, p);
@@ -507,7 +507,10 @@ int launch_alt(const Maps& m, const Params& p, int64_t units, cudaStream_t st) {
 
 template <int D, typename OutT>
 int dispatch_flags(const AttnArgs& a, const Maps& m, const Params& p, int64_t units, cudaStream_t st) {
-  if (a.expcast && !a.block_values && !use_general_kernel()) return launch_alt<D, OutT>(m, p, units, st);
+  if (a.expcast && !a.vs_per_block && !use_general_kernel()) {
+    if (a.block_values) return launch_alt<D, OutT, true>(m, p, units, st);
+    return launch_alt<D, OutT, false>(m, p, units, st);
+  }
   const CUtensorMap& mk = m.k;
   const CUtensorMap& mv = m.v;
   if (a.expcast) {

@@ -1,5 +1,5 @@
-// Alternating-tile fused attention kernel (ExpCast, channel-scaled V, no
-// block means): the default kernel for that mode.  Included by attention.cu
+// Alternating-tile fused attention kernel (ExpCast, channel-scaled V, with or
+// without 128-token block means): the default kernel for those modes.  Included by attention.cu
 // after attention_softmax.cuh (register-level helpers).
 //
 // One CTA owns one 128-row Q tile of a (batch, head).  Warp roles (384 thr):
@@ -26,9 +26,23 @@
 //                             accumulates P.1 (the ExpCast denominator) via a
 //                             row of E4M3 1.0 appended to every V tile
 //   P0 [400,432) P1 [432,464) ExpCast bytes of tiles j%2 (A operand of P.V)
+//   Mt [464,480)              block means only: column 464 receives the tile's
+//                             row mass P(j).1 (an N=16 MMA against the ones
+//                             row of the V tile)
 //   Q  [480,480+D/4)          int8 Q tile (A operand of Q.K^T)
 // A group whose rows' maximum grew at tile j scales its lanes of O (and the
 // denominator column) after PV(j-1) completes and before it releases P(j).
+//
+// Block means (V smoothing, channel scales): the payload is E4M3 of
+// (V - mean_t)/s, so O needs mass_t * mean_t/s per tile besides P.V.  The
+// group of tile j reads mass_{j-1} from Mt after PV(j-1), scales it by
+// alpha_j (O's rescale at tile j), splits it into FP16 hi + lo (exact to
+// ~2^-22) and writes [hi, lo, 0...] as row r of a 128x16 FP16 operand in
+// shared memory; the means of tile j-1 stand as [mean, mean, 0...] rows of
+// a Dx16 FP16 operand (built by the V producer warp), and one kind::f16
+// MMA (K = 16) adds mass_{j-1} alpha_j mean_{j-1} to O just before PV(j).
+// After the last tile the group of parity T%2 hands over mass_{T-1} the
+// same way and the final means MMA precedes o_final.
 //
 // Barrier phases.  Every parity wait below is unconditional (taken on every
 // tile), so a waiter can never be two phases behind its barrier, and no
@@ -42,7 +56,8 @@
 constexpr int kAltThreads = 384;
 constexpr int kKS = 4;   // K ring depth
 constexpr int kVS = 3;   // V ring depth
-constexpr uint32_t kAColS0 = 0, kAColS1 = 128, kAColO = 256, kAColP0 = 400, kAColP1 = 432, kAColQ = 480;
+constexpr uint32_t kAColS0 = 0, kAColS1 = 128, kAColO = 256, kAColP0 = 400, kAColP1 = 432, kAColMt = 464,
+                   kAColQ = 480;
 // Magic addends that leave the ExpCast code (0..128) in the low byte of a
 // float's bits (ulp 1/128 on [2^16, 2^17)).  Byte k of a P word comes from
 // element k; with these addends the weighted sum
@@ -58,6 +73,7 @@ struct __align__(8) AltBarriers {
   uint64_t q_ready, s_full[2], s_free[2], p_full[2], o_final;
   uint64_t pv_done[2];      // PV(i) completes pv_done[(i+1)&1]: the group of tile i+1 waits on it
   uint64_t m_ready[2][4];   // [tile parity][warp of the group]
+  uint64_t mean_full[kVS], mean_empty[kVS];   // block means: the Dx16 FP16 means operand ring
 };
 
 template <int D>
@@ -67,13 +83,21 @@ struct AltSmem {
   static constexpr int kOffK = 0;
   static constexpr int kOffV = kOffK + kKS * kK;
   static constexpr int kOffM = kOffV + kVS * kV;  // float [2][128] running maxima
-  static constexpr int kOffBar = kOffM + 2 * 128 * 4;
+  // block means: FP16 operands without swizzle, rows of 32 bytes (K = 16),
+  // 8-row groups 256 bytes apart, the two K halves 128 bytes apart
+  static constexpr int kOffMassA = kOffM + 2 * 128 * 4;   // 128 x 16 FP16 (mass hi, lo)
+  static constexpr int kMean = D * 32;                     // D x 16 FP16 (mean, mean)
+  static constexpr int kOffMean = kOffMassA + 128 * 32;
+  static constexpr int kOffBar = kOffMean + kVS * kMean;
   static constexpr int kOffSlot = kOffBar + int(sizeof(AltBarriers));
   static constexpr int kBytes = kOffSlot + 16;
   static constexpr int kAlloc = kBytes + 1024;
 };
 
-template <int D, typename OutT>
+// Byte offset of (row, first K element) in the no-swizzle 32-byte-row layout.
+__device__ __forceinline__ int plain32_offset(int r) { return (r >> 3) * 256 + (r & 7) * 16; }
+
+template <int D, typename OutT, bool BV>
 __global__ void __launch_bounds__(kAltThreads, 1)
     vc_attention_alt_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                             Params p) {
@@ -107,6 +131,10 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       mbar_init(&bar->pv_done[b], 1);
       for (int q = 0; q < 4; ++q) mbar_init(&bar->m_ready[b][q], 32);
     }
+    for (int s = 0; s < kVS; ++s) {
+      mbar_init(&bar->mean_full[s], 32);
+      mbar_init(&bar->mean_empty[s], 1);
+    }
     mbar_init(&bar->o_final, 1);
     fence_barrier_init();
   }
@@ -114,6 +142,11 @@ __global__ void __launch_bounds__(kAltThreads, 1)
     const int s = i / (16 * 8), r = (i / 8) % 16, c = i % 8;
     const uint32_t fill = r == 0 ? 0x38383838u : 0u;   // E4M3 1.0 in row D, zeros below
     *reinterpret_cast<uint4*>(smem + L::kOffV + s * L::kV + (D + r) * 128 + c * 16) = make_uint4(fill, fill, fill, fill);
+  }
+  if constexpr (BV) {
+    // zero the FP16 operands once: per tile only the first K pair of a row changes
+    for (int i = threadIdx.x; i < (128 * 32 + kVS * L::kMean) / 16; i += kAltThreads)
+      *reinterpret_cast<uint4*>(smem + L::kOffMassA + i * 16) = make_uint4(0, 0, 0, 0);
   }
   fence_proxy_async_smem();
   if (warp == 9) {
@@ -137,13 +170,37 @@ __global__ void __launch_bounds__(kAltThreads, 1)
         mbar_expect_tx(&bar->k_full[s], L::kK);
         tma_load_3d(smem + L::kOffK + s * L::kK, &tmk, &bar->k_full[s], 0, j * 128, static_cast<int>(bh));
       }
-    } else if (warp == 10 && lane == 0) {
+    } else if (warp == 10 && !BV && lane == 0) {
       // ---------------------------------------------------------- V producer
       for (int j = 0; j < T; ++j) {
         const int s = j % kVS;
         if (j >= kVS && !mbar_wait(&bar->v_empty[s], ((j / kVS) & 1) ^ 1, kErrTimeoutProducer)) break;
         mbar_expect_tx(&bar->v_full[s], D * 128);
         tma_load_3d(smem + L::kOffV + s * L::kV, &tmv, &bar->v_full[s], j * 128, 0, static_cast<int>(bh));
+      }
+    } else if (warp == 10 && BV) {
+      // ------------------------------------- V producer + means operand (warp)
+      // lane l writes channels [l*D/32, (l+1)*D/32) of the tile's means
+      constexpr int CPL = D / 32;
+      for (int j = 0; j < T; ++j) {
+        const int s = j % kVS;
+        if (j >= kVS) {
+          if (!mbar_wait_warp(&bar->v_empty[s], ((j / kVS) & 1) ^ 1, kErrTimeoutProducer)) break;
+          if (!mbar_wait_warp(&bar->mean_empty[s], ((j / kVS) & 1) ^ 1, kErrTimeoutProducer)) break;
+        }
+        if (lane == 0) {
+          mbar_expect_tx(&bar->v_full[s], D * 128);
+          tma_load_3d(smem + L::kOffV + s * L::kV, &tmv, &bar->v_full[s], j * 128, 0, static_cast<int>(bh));
+        }
+        const uint16_t* mrow = reinterpret_cast<const uint16_t*>(p.means) + (bh * T + j) * D + lane * CPL;
+        uint8_t* mop = smem + L::kOffMean + s * L::kMean;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+          const uint32_t m16 = __ldg(mrow + c);
+          *reinterpret_cast<uint32_t*>(mop + plain32_offset(lane * CPL + c)) = m16 | (m16 << 16);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&bar->mean_full[s]);
       }
     } else if (warp == 9 && lane == 0) {
       // ------------------------------------------------------- QK^T issuer
@@ -173,22 +230,52 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       // PV(j) goes as soon as P(j) and V(j) are ready; P has its own TMEM
       // buffers, so this thread never waits on the QK^T issuer.
       constexpr uint32_t idesc_pv = idesc_make(1, 0, 0, 128, D + 16);  // f32 <- e4m3 x e4m3
+      constexpr uint32_t idesc_mass = idesc_make(1, 0, 0, 128, 16);    // f32 <- e4m3 x e4m3
+      constexpr uint32_t idesc_mean = idesc_make(1, 0, 0, 128, D);     // f32 <- f16 x f16
       const uint64_t vdesc0 = smem_desc_sw128(smem_u32(smem + L::kOffV));
       constexpr uint64_t kStepV = (L::kV >> 4);
+      const uint64_t massdesc = smem_desc_plain(smem_u32(smem + L::kOffMassA), 128, 256);
+      const uint64_t meandesc0 = smem_desc_plain(smem_u32(smem + L::kOffMean), 128, 256);
+      constexpr uint64_t kStepMean = (L::kMean >> 4);
       bool ok = true;
       for (int j = 0; j < T && ok; ++j) {
         const int s = j % kVS, b = j & 1;
         ok = mbar_wait(&bar->p_full[b], (j >> 1) & 1, kErrTimeoutMma) &&
              mbar_wait(&bar->v_full[s], (j / kVS) & 1, kErrTimeoutMma);
+        if (BV && ok && j >= 1)
+          ok = mbar_wait(&bar->mean_full[(j - 1) % kVS], ((j - 1) / kVS) & 1, kErrTimeoutMma);
         if (!ok) break;
         tc_fence_after();
+        if constexpr (BV) {
+          if (j >= 1) {   // O += (mass_{j-1} alpha_j) x mean_{j-1}, written by the group of tile j
+            mma_f16_ss(tmem + kAColO, massdesc, meandesc0 + ((j - 1) % kVS) * kStepMean, idesc_mean, 1u);
+            mma_commit(&bar->mean_empty[(j - 1) % kVS]);
+          }
+        }
         const uint64_t vd = vdesc0 + s * kStepV;
         const uint32_t pcol = tmem + (b ? kAColP1 : kAColP0);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           mma_f8_ts(tmem + kAColO, pcol + kk * 8, vd + 2 * kk, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        if constexpr (BV) {
+          // mass_j = P(j).1 against the ones row of the V tile (rows D..D+15)
+          const uint64_t vones = vd + ((D * 128) >> 4);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_f8_ts(tmem + kAColMt, pcol + kk * 8, vones + 2 * kk, idesc_mass, kk > 0 ? 1u : 0u);
+        }
         mma_commit(&bar->v_empty[s]);
         mma_commit(&bar->pv_done[(j + 1) & 1]);
+      }
+      if constexpr (BV) {
+        // the last tile's means: mass_{T-1} comes from the group of parity T%2
+        if (ok) ok = mbar_wait(&bar->p_full[T & 1], (T >> 1) & 1, kErrTimeoutMma) &&
+                     mbar_wait(&bar->mean_full[(T - 1) % kVS], ((T - 1) / kVS) & 1, kErrTimeoutMma);
+        if (ok) {
+          tc_fence_after();
+          mma_f16_ss(tmem + kAColO, massdesc, meandesc0 + ((T - 1) % kVS) * kStepMean, idesc_mean, 1u);
+          mma_commit(&bar->mean_empty[(T - 1) % kVS]);
+        }
       }
       if (ok) mma_commit(&bar->o_final);
     }
@@ -325,9 +412,15 @@ __global__ void __launch_bounds__(kAltThreads, 1)
         }
       }
       // PV(j-1) complete (hence PV(j-2) too): P[b] is free and O may be rescaled
+      float mass_prev = 0.f;   // block means: mass_{j-1} (Mt after PV(j-1))
       if (j >= 1) {
         ok = mbar_wait_warp(&bar->pv_done[b], ((j - 1) >> 1) & 1, kErrTimeoutSoftmax);
         if (!ok) break;
+        if constexpr (BV) {
+          tc_fence_after();
+          mass_prev = __uint_as_float(tmem_ld1(tmem + lane_base + kAColMt));
+          tmem_wait_ld();
+        }
       }
       // rescale O (and the denominator column) between PV(j-1) and PV(j) if any max grew
       if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
@@ -349,12 +442,40 @@ __global__ void __launch_bounds__(kAltThreads, 1)
         for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__fmul_rn(__uint_as_float(o[i]), alpha));
         tmem_st16(ocol + D, o);
       }
+      if constexpr (BV) {
+        if (j >= 1) {   // mass_{j-1} alpha_j as FP16 hi + lo: row t of the means MMA's A operand
+          const float ms = __fmul_rn(mass_prev, alpha);
+          const __half hi = __float2half_rn(ms);
+          const __half lo = __float2half_rn(__fsub_rn(ms, __half2float(hi)));
+          *reinterpret_cast<uint32_t*>(smem + L::kOffMassA + plain32_offset(t)) =
+              static_cast<uint32_t>(__half_as_ushort(hi)) | (static_cast<uint32_t>(__half_as_ushort(lo)) << 16);
+          fence_proxy_async_smem();
+        }
+      }
       // P(j) into this group's P buffer (PV(j-2) has consumed it, see above)
       tc_fence_after();
       tmem_st32(tmem + lane_base + (b ? kAColP1 : kAColP0), pw);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bar->p_full[b]);
+    }
+    if constexpr (BV) {
+      // the group of parity T%2 hands over mass_{T-1} for the last means MMA
+      if (ok && (T & 1) == w) {
+        ok = mbar_wait_warp(&bar->pv_done[T & 1], ((T - 1) >> 1) & 1, kErrTimeoutSoftmax);
+        if (ok) {
+          tc_fence_after();
+          const float ms = __uint_as_float(tmem_ld1(tmem + lane_base + kAColMt));
+          tmem_wait_ld();
+          const __half hi = __float2half_rn(ms);
+          const __half lo = __float2half_rn(__fsub_rn(ms, __half2float(hi)));
+          *reinterpret_cast<uint32_t*>(smem + L::kOffMassA + plain32_offset(t)) =
+              static_cast<uint32_t>(__half_as_ushort(hi)) | (static_cast<uint32_t>(__half_as_ushort(lo)) << 16);
+          fence_proxy_async_smem();
+          tc_fence_before();
+          mbar_arrive(&bar->p_full[T & 1]);
+        }
+      }
     }
     // epilogue: group w writes output channels [w*D/2, (w+1)*D/2)
     if (ok) ok = mbar_wait_warp(&bar->o_final, 0, kErrTimeoutSoftmax);

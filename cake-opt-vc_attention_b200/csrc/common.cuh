@@ -305,6 +305,14 @@ __device__ __forceinline__ void mma_f8_ts(uint32_t d, uint32_t a, uint64_t bdesc
       "r"(a), "l"(bdesc), "r"(idesc), "r"(acc)
       : "memory");
 }
+// D[tmem] (+)= A[smem desc] * B[smem desc], kind::f16 (f16 inputs, f32 accumulate).
+__device__ __forceinline__ void mma_f16_ss(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
 // Arrive on ``bar`` once all previously issued tcgen05 ops of this thread finish.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -324,6 +332,11 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
+}
+__device__ __forceinline__ uint32_t tmem_ld1(uint32_t taddr) {
+  uint32_t r;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+  return r;
 }
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
   asm volatile(
@@ -381,6 +394,17 @@ __device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr) {
   d |= static_cast<uint64_t>(1u) << 46;
   d |= static_cast<uint64_t>(4u) << 61;                 // SWIZZLE_64B
   return d;
+}
+
+// K-major operand without swizzle: 8-row x 16-byte core matrices, ``lbo``
+// bytes between core matrices along K, ``sbo`` bytes between 8-row groups.
+__device__ __forceinline__ uint64_t smem_desc_plain(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;                 // descriptor version for sm_100
+  return d;                                             // layout 0: no swizzle
 }
 
 // UMMA instruction descriptor: dense, K-major A and B, M=128.

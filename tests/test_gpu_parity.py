@@ -265,6 +265,11 @@ ATT_CASES = [
     ("smooth_block_d64", (2, 1, 257, 64), torch.float16, 1.0, True, True, "block"),
     ("control_no_expcast", (1, 1, 129, 128), torch.bfloat16, 1.0, False, False, "channel"),
     ("control_smooth", (1, 1, 260, 64), torch.bfloat16, 1.0, False, True, "channel"),
+    # block means on the tensor-memory kernel: odd / even / single tile counts, D 64 and 128
+    ("smooth_channel_1tile", (1, 1, 100, 128), torch.bfloat16, 1.0, True, True, "channel"),
+    ("smooth_channel_2tiles", (1, 2, 256, 128), torch.bfloat16, 1.0, True, True, "channel"),
+    ("smooth_channel_d64_odd", (2, 1, 645, 64), torch.float16, 1.0, True, True, "channel"),
+    ("smooth_channel_long", (1, 1, 3000, 128), torch.bfloat16, 3 ** 0.5, True, True, "channel"),
 ]
 
 
@@ -346,6 +351,33 @@ def test_attention_is_bitwise_repeatable(ops, sm_scale):
     first = ops.attention_fwd(*args, **kw)
     for _ in range(6):
         assert torch.equal(ops.attention_fwd(*args, **kw), first)
+
+
+@pytest.mark.parametrize("shape", [(1, 2, 1000, 128), (2, 1, 385, 64), (1, 1, 129, 128)])
+@pytest.mark.parametrize("sm_scale", [None, 1.0])
+def test_block_means_fast_and_general_agree(ops, monkeypatch, shape, sm_scale):
+    """Block means (V smoothing, channel scales): the tensor-memory kernel
+    (per-tile mass MMA + FP16 hi/lo means MMA) and the register-accumulating
+    general kernel both meet the tolerance against the oracle, and the fast
+    kernel is bitwise repeatable."""
+    q, k, _ = qk_inputs(35, shape, torch.bfloat16, 3 ** 0.5)
+    v = mixture_values(35, shape, torch.bfloat16)
+    perm = ops.group_values(v.cuda(), 8, 2).cpu()
+    st = _device_state(ops, q, k, v, v_smooth=True, perm=perm)
+    scale = st["scale"] if sm_scale is None else sm_scale
+    args = (st["q"], st["qs"], st["k"], st["ks"], st["v"], st["vs"], st["means"])
+    kw = dict(out_dtype=torch.float32, sm_scale=scale, block_values=True)
+    fast = ops.attention_fwd(*args, **kw)
+    for _ in range(3):
+        assert torch.equal(ops.attention_fwd(*args, **kw), fast)
+    exact = ops.attention_fwd(*args, expcast="exact", **kw)
+    monkeypatch.setenv("VC_B200_KERNEL", "general")
+    general = ops.attention_fwd(*args, **kw)
+    monkeypatch.delenv("VC_B200_KERNEL")
+    ref = O.reference({**_cpu_state(st), "scale": scale})
+    for out in (fast, exact, general):
+        m = O.metrics(out.cpu(), ref)
+        assert m["cos"] >= COS_MIN and m["rel_l2"] <= REL_MAX, m
 
 
 def test_attention_large_logits_and_rescales(ops):
