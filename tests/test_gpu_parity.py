@@ -5,6 +5,7 @@ cos >= 0.9999 and rel-L2 <= 1e-3 of the decoded-payload oracle (the
 tolerance stated by the reference's north star), also reported against FP32
 dense softmax attention.
 """
+import json
 from pathlib import Path
 
 import numpy as np
@@ -432,3 +433,52 @@ def test_sageattn_vc_smooth_end_to_end(ops):
     dense = O.dense_attention(q, k, v)
     m = O.metrics(out.float().cpu(), dense)
     assert m["rel_l2"] < 0.08, m
+
+
+@pytest.mark.parametrize("name", ["c1_cfg_expcast", "cfg_smooth"])
+def test_config_api_sm100a_against_reference_backend(ops, name):
+    """Boundary A: vc_attention.attention(Config(backend="sm100a")) against the
+    reference package's own reference backend on the same inputs.  The QK
+    quantisers differ (Sage INT8 here, E4M3 blocks there), so this is a
+    tolerance check: close to the reference output and as close to FP32
+    dense attention as the reference backend is."""
+    from vc_attention import Config, attention
+    f = np.load(GOLDEN / f"{name}.npz")
+    kw = json.loads(str(f["config"]))
+    shape = tuple(int(x) for x in f["shape"])
+    q, k, v = qk_inputs(int(f["seed"]), shape, torch.float32, float(f["koff"]))
+    out, counters = attention(q.cuda(), k.cuda(), v.cuda(), Config(backend="sm100a", **kw))
+    ref = torch.from_numpy(f["out"])
+    assert out.dtype == torch.float32 and out.shape == ref.shape
+    m = O.metrics(out.cpu(), ref)
+    assert m["cos"] >= 0.998, m
+    dense = O.dense_attention(q, k, v)
+    ours, theirs = O.metrics(out.cpu(), dense), O.metrics(ref, dense)
+    assert ours["rel_l2"] <= 1.25 * theirs["rel_l2"] + 2e-3, (ours, theirs)
+    expected = json.loads((GOLDEN / "manifest.json").read_text())[name]["counters"]
+    for key in ("smoothing_active", "layout_refreshed", "expcast", "k_smooth", "qk_hadamard",
+                "numerical_contract_version", "tiles"):
+        assert counters[key] == expected[key], key
+    assert counters["backend"] == "sm100a" and counters["native_fused_attention"]
+
+
+def test_config_api_layout_cache_across_denoising_steps(ops):
+    """A request of 8 steps: smoothing (grouping + block means) for the first
+    two, layout refreshed at step 0 only, the cached permutation kept after;
+    every step stays close to dense attention."""
+    from vc_attention import Config, LayoutCache, attention
+    shape = (1, 2, 700, 128)
+    q, k, _ = qk_inputs(41, shape, torch.bfloat16, 3 ** 0.5)
+    v = mixture_values(41, shape, torch.bfloat16)
+    cfg = Config(backend="sm100a", qk_hadamard=False, expcast=True, v_smooth=True, refresh_interval=4)
+    cache = LayoutCache(cfg)
+    dense = O.dense_attention(q.float(), k.float(), v.float())
+    flags = []
+    for step in range(8):
+        out, c = attention(q.cuda(), k.cuda(), v.cuda(), cfg, cache=cache, step=step, total_steps=8,
+                           request_id="req", layer_id=3)
+        flags.append((c["smoothing_active"], c["layout_refreshed"]))
+        m = O.metrics(out.float().cpu(), dense)
+        assert m["cos"] >= 0.998, (step, m)
+    assert flags == [(True, True), (True, False)] + [(False, False)] * 6
+    assert cache.entries == 1
