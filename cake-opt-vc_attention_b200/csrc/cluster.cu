@@ -67,7 +67,8 @@ __global__ void __launch_bounds__(128) grp_assign(const T* __restrict__ v, int64
   const int64_t bh = blockIdx.y, tile = blockIdx.x;
   const int64_t b = bh / H, h = bh - b * H;
   const int lane = threadIdx.x & 3, group = threadIdx.x >> 2;
-  for (int i = threadIdx.x; i < count * D; i += 128) cen[i / D][i % D] = centers[bh * count * D + i];
+  for (int i = threadIdx.x; i < kMaxC * D; i += 128)
+    cen[i / D][i % D] = i < count * D ? centers[bh * count * D + i] : 0.f;
   // stage the tile as FP32 (zeros past S)
   constexpr int EPT = 16 / sizeof(T);
   constexpr int CPR = D / EPT;
@@ -87,7 +88,7 @@ __global__ void __launch_bounds__(128) grp_assign(const T* __restrict__ v, int64
   __syncthreads();
   {
     float cn = 0.f;
-    if (group < count) {
+    if (group < kMaxC) {
 #pragma unroll 8
       for (int j = 0; j < D / 4; ++j) {
         const float x = cen[group][j * 4 + lane];
@@ -95,28 +96,33 @@ __global__ void __launch_bounds__(128) grp_assign(const T* __restrict__ v, int64
       }
     }
     cn = sum_four(cn);
-    if (group < count && lane == 0) cnorm[group] = cn;
+    if (group < kMaxC && lane == 0) cnorm[group] = cn;
   }
   __syncthreads();
   for (int off = 0; off < kRows; off += 32) {
     const int r = off + group;
     const int64_t row = tile * kRows + r;
+    // all centres' dot products advance together (8 independent FMA chains);
+    // each one still sums its lane's elements in the same order
     float norm = 0.f;
-#pragma unroll 8
+    float dot[kMaxC];
+#pragma unroll
+    for (int c = 0; c < kMaxC; ++c) dot[c] = 0.f;
+#pragma unroll 4
     for (int j = 0; j < D / 4; ++j) {
       const float x = xs[r][j * 4 + lane];
       norm = __fadd_rn(norm, __fmul_rn(x, x));
+#pragma unroll
+      for (int c = 0; c < kMaxC; ++c) dot[c] = __fmaf_rn(x, cen[c][j * 4 + lane], dot[c]);
     }
     norm = sum_four(norm);
     float best_d = __int_as_float(0x7f800000);
     int best = 0;
-    for (int c = 0; c < count; ++c) {
-      float dot = 0.f;
-#pragma unroll 8
-      for (int j = 0; j < D / 4; ++j) dot = __fmaf_rn(xs[r][j * 4 + lane], cen[c][j * 4 + lane], dot);
-      dot = sum_four(dot);
-      const float dist = __fsub_rn(__fadd_rn(norm, cnorm[c]), __fmul_rn(2.f, dot));
-      if (dist < best_d) {
+#pragma unroll
+    for (int c = 0; c < kMaxC; ++c) {
+      const float dc = sum_four(dot[c]);
+      const float dist = __fsub_rn(__fadd_rn(norm, cnorm[c]), __fmul_rn(2.f, dc));
+      if (c < count && dist < best_d) {
         best_d = dist;
         best = c;
       }
@@ -140,7 +146,9 @@ __global__ void __launch_bounds__(128) grp_assign(const T* __restrict__ v, int64
         for (int cc = 0; cc < kMaxC; ++cc)
           if (cc == c) acc[cc] = __fadd_rn(acc[cc], x);
       }
-      for (int c = 0; c < count; ++c) psum[((bh * tiles + tile) * count + c) * D + d] = acc[c];
+#pragma unroll
+      for (int c = 0; c < kMaxC; ++c)
+        if (c < count) psum[((bh * tiles + tile) * count + c) * D + d] = acc[c];
     }
     if (threadIdx.x < count) {
       int n = 0;
