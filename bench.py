@@ -326,13 +326,14 @@ def main():
         hout = torch.empty((1, nbh, S, D), dtype=dtype).pin_memory()
 
         def e2e_step():
-            dq, dk, dv = (x.to(dev, non_blocking=True) for x in (hq, hk, hv))
             if world == 1:
-                from sageattention_local import sageattn_vc
-                o = sageattn_vc(dq, dk, dv, v_smooth=smooth)
+                # public host-tensor API: per-head-chunk copies overlapped with the computation
+                from vc_b200.pipeline import sageattn_vc_host
+                sageattn_vc_host(hq, hk, hv, hout, device=dev, v_smooth=smooth)
             else:
+                dq, dk, dv = (x.to(dev, non_blocking=True) for x in (hq, hk, hv))
                 o = parallel.sharded_attention(dq, dk, dv, local_shard, v_smooth=smooth)
-            hout.copy_(o, non_blocking=True)
+                hout.copy_(o, non_blocking=True)
 
         for _ in range(2):
             e2e_step()
@@ -354,7 +355,8 @@ def main():
         e2e = {"value": ops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": 3 * nbh * S * D * q.element_size(),
                "d2h_bytes_per_step": nbh * S * D * q.element_size(),
-               "path": "sageattn_vc(q,k,v) on pinned-host inputs (per-rank shard for N>1)"}
+               "path": ("vc_b200.pipeline.sageattn_vc_host on pinned-host inputs (head chunks, copies overlapped)"
+                        if world == 1 else "per-rank sharded_attention on pinned-host inputs")}
 
     gather_ms = None
     if args.gather and dist:

@@ -482,3 +482,18 @@ def test_config_api_layout_cache_across_denoising_steps(ops):
         assert m["cos"] >= 0.998, (step, m)
     assert flags == [(True, True), (True, False)] + [(False, False)] * 6
     assert cache.entries == 1
+
+
+@pytest.mark.parametrize("smooth", [False, True])
+def test_host_pipeline_equals_one_call(ops, smooth):
+    """sageattn_vc_host (head chunks, PCIe copies overlapped) gives the bits of
+    one sageattn_vc call on the device tensors."""
+    from sageattention_local import sageattn_vc
+    from vc_b200.pipeline import sageattn_vc_host
+    shape = (2, 5, 700, 128)
+    q, k, _ = qk_inputs(43, shape, torch.bfloat16, 3 ** 0.5)
+    v = mixture_values(43, shape, torch.bfloat16)
+    hq, hk, hv = (x.pin_memory() for x in (q, k, v))
+    got = sageattn_vc_host(hq, hk, hv, chunk_heads=3, v_smooth=smooth)
+    want = sageattn_vc(q.cuda(), k.cuda(), v.cuda(), v_smooth=smooth)
+    assert got.device.type == "cpu" and torch.equal(got, want.cpu())
