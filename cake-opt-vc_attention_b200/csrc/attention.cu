@@ -59,9 +59,6 @@ struct Params {
   int64_t unit_begin, unit_end;   // units (b*H+h)*qtiles + q_tile to compute
   float sm_scale;
   int exact_expcast;   // 1: unfused RN(RN(raw*f)-m) encoder instead of the folded affine one
-  // 2^8, 2^16, 2^24 as launch arguments: the byte packing multiplies by them
-  // (integer multiply-add on the FMA pipe) instead of shifting on the ALU pipe
-  uint32_t mul8, mul16, mul24;
 };
 
 struct __align__(8) Barriers {
@@ -564,9 +561,6 @@ int attention_fwd(const AttnArgs& a, cudaStream_t st) {
   p.unit_end = ue;
   p.sm_scale = a.sm_scale;
   p.exact_expcast = a.expcast == 2 ? 1 : 0;
-  p.mul8 = 1u << 8;
-  p.mul16 = 1u << 16;
-  p.mul24 = 1u << 24;
   const int64_t units = ue - ub;
   if (a.out_dtype == VC_DTYPE_BF16)
     return a.D == 128 ? dispatch_flags<128, __nv_bfloat16>(a, m, p, units, st)

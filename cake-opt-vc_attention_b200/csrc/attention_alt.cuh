@@ -58,15 +58,13 @@ constexpr int kKS = 4;   // K ring depth
 constexpr int kVS = 3;   // V ring depth
 constexpr uint32_t kAColS0 = 0, kAColS1 = 128, kAColO = 256, kAColP0 = 400, kAColP1 = 432, kAColMt = 464,
                    kAColQ = 480;
-// Magic addends that leave the ExpCast code (0..128) in the low byte of a
-// float's bits (ulp 1/128 on [2^16, 2^17)).  Byte k of a P word comes from
-// element k; with these addends the weighted sum
-//   bits(e0 + kMagFirst) + 2^8 bits(e1 + kMagRest) + 2^16 bits(e2 + kMagRest)
-//                        + 2^24 bits(e3 + kMagRest)         (mod 2^32)
-// is exactly the packed code word, because
-//   0x47C80000 + 0x47803800 * 0x01010100 == 0 (mod 2^32).
-constexpr float kMagFirst = 102400.0f;   // bits 0x47C80000
-constexpr float kMagRest = 65648.0f;     // bits 0x47803800
+// ExpCast code of an FP32 argument u (already rounded by its FMA): u * 2^-149
+// lands on the denormal grid, whose round-to-nearest-even gives the bit
+// pattern RNE(u) for 0 <= u < 2^23 and a negative (sign-bit) pattern for
+// u < 0; cvt.pack.sat.u8.s32 then clamps to [0, 255] (u <= 120.5 here, as
+// s <= m) and packs two codes per instruction.  No conversion-unit work, no
+// explicit clamp.
+constexpr uint32_t kDenormOne = 1u;   // bits of 2^-149
 
 struct __align__(8) AltBarriers {
   uint64_t k_full[kKS], k_empty[kKS], v_full[kVS], v_empty[kVS];
@@ -305,8 +303,8 @@ __global__ void __launch_bounds__(kAltThreads, 1)
     const float qscale = row_valid ? p.qs[bh * p.nqs + (row >> 4) * 8 + (row & 7)] : 0.f;
     const float scale = p.sm_scale;
     const uint64_t bias2 = pk2f(kBias, kBias);
-    const uint64_t magA = pk2f(kMagFirst, kMagRest), magB = pk2f(kMagRest, kMagRest);
-    const uint32_t mul8 = p.mul8, mul16 = p.mul16, mul24 = p.mul24;
+    const uint64_t tiny2 = pk2(kDenormOne, kDenormOne);
+    const uint64_t expa2 = pk2f(kExpA, kExpA), expb2 = pk2f(kExpB, kExpB);
     {
       // preset this group's score buffer S[w] for its first tile
       const uint32_t scol = tmem + lane_base + (w ? kAColS1 : kAColS0);
@@ -372,43 +370,43 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       uint32_t pw[32];
       float gain[4];
 #pragma unroll
-      for (int g = 0; g < 4; ++g) gain[g] = __fmul_rn(f1[g], kExpA) * (1.0f / 128.0f);
-      const float cb = __fmaf_rn(-mn, kExpA, kExpB) * (1.0f / 128.0f);
+      for (int g = 0; g < 4; ++g) gain[g] = __fmul_rn(f1[g], kExpA);
+      const float cb = __fmaf_rn(-mn, kExpA, kExpB);
       const bool safe = !p.exact_expcast && fabsf(mn) <= 128.f && scale >= 1.1754943508222875e-38f &&
                         isfinite(gain[0]) && isfinite(gain[1]) && isfinite(gain[2]) && isfinite(gain[3]);
       if (__all_sync(0xffffffffu, safe)) {
 #pragma unroll
+        uint64_t gain2[4];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) gain2[g] = pk2f(gain[g], gain[g]);
+        const uint64_t cb2 = pk2f(cb, cb);
+#pragma unroll
         for (int wd = 0; wd < 32; ++wd) {
-          uint32_t fw[4];
+          uint32_t e[4];
 #pragma unroll
           for (int q2 = 0; q2 < 2; ++q2) {
             const int c = 4 * wd + 2 * q2;
             const int g = (c >> 1) & 3;
-            uint32_t a, bb;
-            up2(f2_sub(pk2(raw[c], raw[c + 1]), bias2), a, bb);
-            const float va = fma_sat(__uint_as_float(a), gain[g], cb);
-            const float vb = fma_sat(__uint_as_float(bb), gain[g], cb);
-            up2(f2_add(pk2f(va, vb), q2 ? magB : magA), fw[2 * q2], fw[2 * q2 + 1]);
+            // u = fma(float(raw), RN(f A), fma(-m, A, B)) (the folded affine encoder)
+            const uint64_t u2 = f2_fma(f2_sub(pk2(raw[c], raw[c + 1]), bias2), gain2[g], cb2);
+            up2(f2_mul(u2, tiny2), e[2 * q2], e[2 * q2 + 1]);
           }
-          pw[wd] = fw[0] + fw[1] * mul8 + fw[2] * mul16 + fw[3] * mul24;
+          pw[wd] = pack_u8x2(e[1], e[0], pack_u8x2(e[3], e[2], 0u));
         }
       } else {
         const uint64_t m2 = pk2f(mn, mn);
 #pragma unroll
         for (int wd = 0; wd < 32; ++wd) {
-          uint32_t fw[4];
+          uint32_t e[4];
 #pragma unroll
           for (int q2 = 0; q2 < 2; ++q2) {
             const int c = 4 * wd + 2 * q2;
             const int g = (c >> 1) & 3;
+            // u = fma(RN(RN(float(raw) f) - m), A, B) (the unfused contract)
             const uint64_t sh = f2_sub(f2_mul(f2_sub(pk2(raw[c], raw[c + 1]), bias2), pk2f(f1[g], f1[g])), m2);
-            uint32_t a, bb;
-            up2(sh, a, bb);
-            const float va = fma_sat(__uint_as_float(a), kExpA128, kExpB128);
-            const float vb = fma_sat(__uint_as_float(bb), kExpA128, kExpB128);
-            up2(f2_add(pk2f(va, vb), q2 ? magB : magA), fw[2 * q2], fw[2 * q2 + 1]);
+            up2(f2_mul(f2_fma(sh, expa2, expb2), tiny2), e[2 * q2], e[2 * q2 + 1]);
           }
-          pw[wd] = fw[0] + fw[1] * mul8 + fw[2] * mul16 + fw[3] * mul24;
+          pw[wd] = pack_u8x2(e[1], e[0], pack_u8x2(e[3], e[2], 0u));
         }
       }
       // PV(j-1) complete (hence PV(j-2) too): P[b] is free and O may be rescaled
