@@ -424,21 +424,20 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
         tc_fence_after();
         const uint32_t ocol = tmem + lane_base + kAColO;
+        const uint64_t alpha2 = pk2f(alpha, alpha);
 #pragma unroll
         for (int cc = 0; cc < D / 32; ++cc) {
           uint32_t o[32];
           tmem_ld32(ocol + cc * 32, o);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__fmul_rn(__uint_as_float(o[i]), alpha));
+          for (int i = 0; i < 16; ++i) up2(f2_mul(pk2(o[2 * i], o[2 * i + 1]), alpha2), o[2 * i], o[2 * i + 1]);
           tmem_st32(ocol + cc * 32, o);
         }
-        uint32_t o[16];
-        tmem_ld16(ocol + D, o);
+        // the denominator: column D (columns D+1.. of the block only ever hold zeros)
+        const float dn = __uint_as_float(tmem_ld1(ocol + D));
         tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__fmul_rn(__uint_as_float(o[i]), alpha));
-        tmem_st16(ocol + D, o);
+        tmem_st1(ocol + D, __float_as_uint(__fmul_rn(dn, alpha)));
       }
       if constexpr (BV) {
         if (j >= 1) {   // mass_{j-1} alpha_j as FP16 hi + lo: row t of the means MMA's A operand
