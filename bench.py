@@ -372,7 +372,10 @@ def main():
         cpu = cpu_baseline_sample(B, H, S, D, dtype, k_std, smooth)
 
     if rank == 0:
-        launches_per_step = 4 + 2 + 1 + (0 if not smooth else 6)
+        # this library's kernels per step: K sums + mean finalize, Q/K tiles, then V channel amax +
+        # quantise (no smoothing) or grouping (init, 2 assignments, update, histogram, scan, scatter)
+        # + block stats, channel scales, quantise; then the fused attention kernel
+        launches_per_step = (2 + 1 + 2 + 1) if not smooth else (2 + 1 + 7 + 3 + 1)
         line = {"metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "int8 QK / e4m3 PV (fp32 accumulate), bf16 I/O",
