@@ -26,21 +26,22 @@
 //                             accumulates P.1 (the ExpCast denominator) via a
 //                             row of E4M3 1.0 appended to every V tile
 //   P0 [400,432) P1 [432,464) ExpCast bytes of tiles j%2 (A operand of P.V)
-//   Mt [464,480)              block means only: column 464 receives the tile's
-//                             row mass P(j).1 (an N=16 MMA against the ones
-//                             row of the V tile)
 //   Q  [480,480+D/4)          int8 Q tile (A operand of Q.K^T)
 // A group whose rows' maximum grew at tile j scales its lanes of O (and the
 // denominator column) after PV(j-1) completes and before it releases P(j).
 //
 // Block means (V smoothing, channel scales): the payload is E4M3 of
 // (V - mean_t)/s, so O needs mass_t * mean_t/s per tile besides P.V.  The
-// group of tile j reads mass_{j-1} from Mt after PV(j-1), scales it by
-// alpha_j (O's rescale at tile j), splits it into FP16 hi + lo (exact to
-// ~2^-22) and writes [hi, lo, 0...] as row r of a 128x16 FP16 operand in
-// shared memory; the means of tile j-1 stand as [mean, mean, 0...] rows of
-// a Dx16 FP16 operand (built by the V producer warp), and one kind::f16
-// MMA (K = 16) adds mass_{j-1} alpha_j mean_{j-1} to O just before PV(j).
+// tile masses come from the denominator column: the group of tile j reads
+// column D after PV(j-1) (d_{j-1}), hands d_{j-1} alpha_j -- the column's
+// value just before PV(j) -- to the other group through shared memory, and
+// takes mass_{j-1} = d_{j-1} - (the value handed over for tile j-1).  The
+// difference loses at most an ulp of the running denominator per tile.
+// mass_{j-1} alpha_j is split into FP16 hi + lo (exact to ~2^-22) and
+// written as row r of a 128x16 FP16 operand [hi, lo, 0...] in shared
+// memory; the means of tile j-1 stand as [mean, mean, 0...] rows of a Dx16
+// FP16 operand (built by the V producer warp), and one kind::f16 MMA
+// (K = 16) adds mass_{j-1} alpha_j mean_{j-1} to O just before PV(j).
 // After the last tile the group of parity T%2 hands over mass_{T-1} the
 // same way and the final means MMA precedes o_final.
 //
@@ -56,8 +57,7 @@
 constexpr int kAltThreads = 384;
 constexpr int kKS = 4;   // K ring depth
 constexpr int kVS = 3;   // V ring depth
-constexpr uint32_t kAColS0 = 0, kAColS1 = 128, kAColO = 256, kAColP0 = 400, kAColP1 = 432, kAColMt = 464,
-                   kAColQ = 480;
+constexpr uint32_t kAColS0 = 0, kAColS1 = 128, kAColO = 256, kAColP0 = 400, kAColP1 = 432, kAColQ = 480;
 // ExpCast code of an FP32 argument u (already rounded by its FMA): u * 2^-149
 // lands on the denormal grid, whose round-to-nearest-even gives the bit
 // pattern RNE(u) for 0 <= u < 2^23 and a negative (sign-bit) pattern for
@@ -72,6 +72,7 @@ struct __align__(8) AltBarriers {
   uint64_t pv_done[2];      // PV(i) completes pv_done[(i+1)&1]: the group of tile i+1 waits on it
   uint64_t m_ready[2][4];   // [tile parity][warp of the group]
   uint64_t mean_full[kVS], mean_empty[kVS];   // block means: the Dx16 FP16 means operand ring
+  uint64_t d_ready[2][4];                     // block means: denominator before PV(j) handed over
 };
 
 template <int D>
@@ -83,7 +84,8 @@ struct AltSmem {
   static constexpr int kOffM = kOffV + kVS * kV;  // float [2][128] running maxima
   // block means: FP16 operands without swizzle, rows of 32 bytes (K = 16),
   // 8-row groups 256 bytes apart, the two K halves 128 bytes apart
-  static constexpr int kOffMassA = kOffM + 2 * 128 * 4;   // 128 x 16 FP16 (mass hi, lo)
+  static constexpr int kOffD = kOffM + 2 * 128 * 4;        // float [2][128] denominators before PV(j)
+  static constexpr int kOffMassA = kOffD + 2 * 128 * 4;    // 128 x 16 FP16 (mass hi, lo)
   static constexpr int kMean = D * 32;                     // D x 16 FP16 (mean, mean)
   static constexpr int kOffMean = kOffMassA + 128 * 32;
   static constexpr int kOffBar = kOffMean + kVS * kMean;
@@ -133,6 +135,8 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       mbar_init(&bar->mean_full[s], 32);
       mbar_init(&bar->mean_empty[s], 1);
     }
+    for (int b = 0; b < 2; ++b)
+      for (int q = 0; q < 4; ++q) mbar_init(&bar->d_ready[b][q], 32);
     mbar_init(&bar->o_final, 1);
     fence_barrier_init();
   }
@@ -228,7 +232,6 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       // PV(j) goes as soon as P(j) and V(j) are ready; P has its own TMEM
       // buffers, so this thread never waits on the QK^T issuer.
       constexpr uint32_t idesc_pv = idesc_make(1, 0, 0, 128, D + 16);  // f32 <- e4m3 x e4m3
-      constexpr uint32_t idesc_mass = idesc_make(1, 0, 0, 128, 16);    // f32 <- e4m3 x e4m3
       constexpr uint32_t idesc_mean = idesc_make(1, 0, 0, 128, D);     // f32 <- f16 x f16
       const uint64_t vdesc0 = smem_desc_sw128(smem_u32(smem + L::kOffV));
       constexpr uint64_t kStepV = (L::kV >> 4);
@@ -255,13 +258,6 @@ __global__ void __launch_bounds__(kAltThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           mma_f8_ts(tmem + kAColO, pcol + kk * 8, vd + 2 * kk, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
-        if constexpr (BV) {
-          // mass_j = P(j).1 against the ones row of the V tile (rows D..D+15)
-          const uint64_t vones = vd + ((D * 128) >> 4);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_f8_ts(tmem + kAColMt, pcol + kk * 8, vones + 2 * kk, idesc_mass, kk > 0 ? 1u : 0u);
-        }
         mma_commit(&bar->v_empty[s]);
         mma_commit(&bar->pv_done[(j + 1) & 1]);
       }
@@ -410,13 +406,13 @@ __global__ void __launch_bounds__(kAltThreads, 1)
         }
       }
       // PV(j-1) complete (hence PV(j-2) too): P[b] is free and O may be rescaled
-      float mass_prev = 0.f;   // block means: mass_{j-1} (Mt after PV(j-1))
+      float dcur = 0.f;   // block means: denominator column after PV(j-1)
       if (j >= 1) {
         ok = mbar_wait_warp(&bar->pv_done[b], ((j - 1) >> 1) & 1, kErrTimeoutSoftmax);
         if (!ok) break;
         if constexpr (BV) {
           tc_fence_after();
-          mass_prev = __uint_as_float(tmem_ld1(tmem + lane_base + kAColMt));
+          dcur = __uint_as_float(tmem_ld1(tmem + lane_base + kAColO + D));
           tmem_wait_ld();
         }
       }
@@ -435,19 +431,28 @@ __global__ void __launch_bounds__(kAltThreads, 1)
           tmem_st32(ocol + cc * 32, o);
         }
         // the denominator: column D (columns D+1.. of the block only ever hold zeros)
-        const float dn = __uint_as_float(tmem_ld1(ocol + D));
-        tmem_wait_ld();
+        float dn = dcur;
+        if constexpr (!BV) {
+          dn = __uint_as_float(tmem_ld1(ocol + D));
+          tmem_wait_ld();
+        }
         tmem_st1(ocol + D, __float_as_uint(__fmul_rn(dn, alpha)));
       }
       if constexpr (BV) {
+        float* dbuf = reinterpret_cast<float*>(smem + L::kOffD);
         if (j >= 1) {   // mass_{j-1} alpha_j as FP16 hi + lo: row t of the means MMA's A operand
-          const float ms = __fmul_rn(mass_prev, alpha);
+          ok = mbar_wait_warp(&bar->d_ready[b ^ 1][quarter], ((j - 1) >> 1) & 1, kErrTimeoutSoftmax);
+          if (!ok) break;
+          const float ms = __fmul_rn(__fsub_rn(dcur, dbuf[(b ^ 1) * 128 + t]), alpha);
           const __half hi = __float2half_rn(ms);
           const __half lo = __float2half_rn(__fsub_rn(ms, __half2float(hi)));
           *reinterpret_cast<uint32_t*>(smem + L::kOffMassA + plain32_offset(t)) =
               static_cast<uint32_t>(__half_as_ushort(hi)) | (static_cast<uint32_t>(__half_as_ushort(lo)) << 16);
           fence_proxy_async_smem();
         }
+        // the denominator column just before PV(j), for the group of tile j+1
+        dbuf[b * 128 + t] = j >= 1 ? __fmul_rn(dcur, alpha) : 0.f;
+        mbar_arrive(&bar->d_ready[b][quarter]);
       }
       // P(j) into this group's P buffer (PV(j-2) has consumed it, see above)
       tc_fence_after();
@@ -459,11 +464,13 @@ __global__ void __launch_bounds__(kAltThreads, 1)
     if constexpr (BV) {
       // the group of parity T%2 hands over mass_{T-1} for the last means MMA
       if (ok && (T & 1) == w) {
-        ok = mbar_wait_warp(&bar->pv_done[T & 1], ((T - 1) >> 1) & 1, kErrTimeoutSoftmax);
+        ok = mbar_wait_warp(&bar->pv_done[T & 1], ((T - 1) >> 1) & 1, kErrTimeoutSoftmax) &&
+             mbar_wait_warp(&bar->d_ready[(T - 1) & 1][quarter], ((T - 1) >> 1) & 1, kErrTimeoutSoftmax);
         if (ok) {
           tc_fence_after();
-          const float ms = __uint_as_float(tmem_ld1(tmem + lane_base + kAColMt));
+          const float dlast = __uint_as_float(tmem_ld1(tmem + lane_base + kAColO + D));
           tmem_wait_ld();
+          const float ms = __fsub_rn(dlast, reinterpret_cast<const float*>(smem + L::kOffD)[((T - 1) & 1) * 128 + t]);
           const __half hi = __float2half_rn(ms);
           const __half lo = __float2half_rn(__fsub_rn(ms, __half2float(hi)));
           *reinterpret_cast<uint32_t*>(smem + L::kOffMassA + plain32_offset(t)) =

@@ -4,8 +4,8 @@
 //
 // Per-score arithmetic of the ExpCast encoders (no conversion-unit work):
 //   float(raw) = as_float(raw + 0x4B400000) - 1.5*2^23    (exact, |raw| < 2^22)
-//   v          = sat(fma(logit-domain value, A/128, B/128))  (= clamp(u,0,128)/128)
-//   byte       = low byte of as_int(v + magic)               (RNE to 1/128)
+//   u          = fma(logit-domain value, A, B)
+//   byte       = sat_u8(bits(u * 2^-149))                    (RNE on the denormal grid)
 #pragma once
 
 __device__ __forceinline__ uint64_t pk2(uint32_t lo, uint32_t hi) {
@@ -16,11 +16,6 @@ __device__ __forceinline__ uint64_t pk2(uint32_t lo, uint32_t hi) {
 __device__ __forceinline__ uint64_t pk2f(float lo, float hi) { return pk2(__float_as_uint(lo), __float_as_uint(hi)); }
 __device__ __forceinline__ void up2(uint64_t v, uint32_t& lo, uint32_t& hi) {
   asm("mov.b64 {%0,%1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
 }
 __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
   uint64_t r;
@@ -43,18 +38,10 @@ __device__ __forceinline__ uint32_t pack_u8x2(uint32_t a, uint32_t b, uint32_t c
   asm("cvt.pack.sat.u8.s32.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
   return d;
 }
-__device__ __forceinline__ float fma_sat(float a, float b, float c) {
-  float r;
-  asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-  return r;
-}
 __device__ __forceinline__ float max3f(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
   return r;
-}
-__device__ __forceinline__ void named_bar(uint32_t id, uint32_t count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -62,9 +49,6 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 constexpr uint32_t kBiasBits = 0x4B400000u;   // 1.5 * 2^23
 constexpr float kBias = 12582912.0f;
-constexpr float kMag = 98304.0f;              // 1.5 * 2^16
-constexpr float kExpA128 = 11.541560173034668f / 128.0f;
-constexpr float kExpB128 = 119.6500015258789f / 128.0f;
 
 template <uint32_t N>
 __device__ __forceinline__ void setmaxnreg_inc() {

@@ -147,20 +147,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Non-blocking probe (never suspends the thread): for event loops that poll
-// several barriers.
-__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n"
-      " mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
 // try_wait with a suspend-time hint: the thread sleeps in hardware until the
 // phase completes or about ``ns`` nanoseconds pass, issuing nothing meanwhile.
 __device__ __forceinline__ bool mbar_try_wait_for(uint32_t bar, uint32_t parity, uint32_t ns) {
@@ -287,14 +273,6 @@ __device__ __forceinline__ void mma_i8_ts(uint32_t d, uint32_t a, uint64_t bdesc
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
       "r"(a), "l"(bdesc), "r"(idesc), "r"(acc)
-      : "memory");
-}
-// D[tmem] (+)= A[smem desc] * B[smem desc], kind::i8 (s32 accumulate).
-__device__ __forceinline__ void mma_i8_ss(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
       : "memory");
 }
 // D[tmem] (+)= A[tmem] * B[smem desc], kind::f8f6f4 (f32 accumulate).
