@@ -37,13 +37,17 @@
 // value just before PV(j) -- to the other group through shared memory, and
 // takes mass_{j-1} = d_{j-1} - (the value handed over for tile j-1).  The
 // difference loses at most an ulp of the running denominator per tile.
-// mass_{j-1} alpha_j is split into FP16 hi + lo (exact to ~2^-22) and
-// written as row r of a 128x16 FP16 operand [hi, lo, 0...] in shared
-// memory; the means of tile j-1 stand as [mean, mean, 0...] rows of a Dx16
-// FP16 operand (built by the V producer warp), and one kind::f16 MMA
-// (K = 16) adds mass_{j-1} alpha_j mean_{j-1} to O just before PV(j).
-// After the last tile the group of parity T%2 hands over mass_{T-1} the
-// same way and the final means MMA precedes o_final.
+// Masses are applied in batches of 8 tiles, one kind::f16 MMA (K = 16) per
+// batch: row r of the 128x16 FP16 A operand holds [hi_0, lo_0, ..., hi_7,
+// lo_7], the FP16 hi + lo split (exact to ~2^-22) of the batch's 8 masses,
+// and channel c of the Dx16 B operand holds [mean_0, mean_0, ..., mean_7,
+// mean_7] (written by the V producer warp, two batch buffers).  Until its
+// batch is applied a mass waits in FP32 in shared memory at O's scale: the
+// group of tile j multiplies the pending masses by alpha_j as it rescales O.
+// The group of tile 8k+8 completes batch k (mass_{8k+7}), writes the A
+// operand, and the batch's MMA goes just before PV(8k+8); after the last
+// tile the group of parity T%2 completes the final, possibly partial, batch
+// (its unused slots zero) and that MMA precedes o_final.
 //
 // Barrier phases.  Every parity wait below is unconditional (taken on every
 // tile), so a waiter can never be two phases behind its barrier, and no
@@ -71,7 +75,7 @@ struct __align__(8) AltBarriers {
   uint64_t q_ready, s_full[2], s_free[2], p_full[2], o_final;
   uint64_t pv_done[2];      // PV(i) completes pv_done[(i+1)&1]: the group of tile i+1 waits on it
   uint64_t m_ready[2][4];   // [tile parity][warp of the group]
-  uint64_t mean_full[kVS], mean_empty[kVS];   // block means: the Dx16 FP16 means operand ring
+  uint64_t mean_full[2];                      // block means: batch buffer k%2 of the means operand written
   uint64_t d_ready[2][4];                     // block means: denominator before PV(j) handed over
 };
 
@@ -85,10 +89,11 @@ struct AltSmem {
   // block means: FP16 operands without swizzle, rows of 32 bytes (K = 16),
   // 8-row groups 256 bytes apart, the two K halves 128 bytes apart
   static constexpr int kOffD = kOffM + 2 * 128 * 4;        // float [2][128] denominators before PV(j)
-  static constexpr int kOffMassA = kOffD + 2 * 128 * 4;    // 128 x 16 FP16 (mass hi, lo)
-  static constexpr int kMean = D * 32;                     // D x 16 FP16 (mean, mean)
-  static constexpr int kOffMean = kOffMassA + 128 * 32;
-  static constexpr int kOffBar = kOffMean + kVS * kMean;
+  static constexpr int kOffPend = kOffD + 2 * 128 * 4;     // float4 [2][128]: row t's 8 pending masses
+  static constexpr int kOffMassA = kOffPend + 2 * 128 * 16;  // 128 x 16 FP16 (mass hi, lo) x 8 tiles
+  static constexpr int kMean = D * 32;                       // D x 16 FP16 (mean, mean) x 8 tiles
+  static constexpr int kOffMean = kOffMassA + 128 * 32;      // two batch buffers
+  static constexpr int kOffBar = kOffMean + 2 * kMean;
   static constexpr int kOffSlot = kOffBar + int(sizeof(AltBarriers));
   static constexpr int kBytes = kOffSlot + 16;
   static constexpr int kAlloc = kBytes + 1024;
@@ -96,6 +101,23 @@ struct AltSmem {
 
 // Byte offset of (row, first K element) in the no-swizzle 32-byte-row layout.
 __device__ __forceinline__ int plain32_offset(int r) { return (r >> 3) * 256 + (r & 7) * 16; }
+
+// Row t of the means MMA's A operand from row t's pending masses: the first
+// n as FP16 hi + lo pairs, the rest zero; then made visible to the MMA.
+__device__ __forceinline__ void write_mass_operand(uint8_t* a, const float4* pend, int t, int n) {
+  const float4 x0 = pend[t], x1 = pend[128 + t];
+  const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+  uint32_t wd[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const __half hi = __float2half_rn(x[i]);
+    const __half lo = __float2half_rn(__fsub_rn(x[i], __half2float(hi)));
+    wd[i] = i < n ? static_cast<uint32_t>(__half_as_ushort(hi)) | (static_cast<uint32_t>(__half_as_ushort(lo)) << 16) : 0u;
+  }
+  *reinterpret_cast<uint4*>(a + plain32_offset(t)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+  *reinterpret_cast<uint4*>(a + plain32_offset(t) + 128) = make_uint4(wd[4], wd[5], wd[6], wd[7]);
+  fence_proxy_async_smem();
+}
 
 template <int D, typename OutT, bool BV>
 __global__ void __launch_bounds__(kAltThreads, 1)
@@ -131,10 +153,7 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       mbar_init(&bar->pv_done[b], 1);
       for (int q = 0; q < 4; ++q) mbar_init(&bar->m_ready[b][q], 32);
     }
-    for (int s = 0; s < kVS; ++s) {
-      mbar_init(&bar->mean_full[s], 32);
-      mbar_init(&bar->mean_empty[s], 1);
-    }
+    for (int s = 0; s < 2; ++s) mbar_init(&bar->mean_full[s], 32);
     for (int b = 0; b < 2; ++b)
       for (int q = 0; q < 4; ++q) mbar_init(&bar->d_ready[b][q], 32);
     mbar_init(&bar->o_final, 1);
@@ -146,9 +165,9 @@ __global__ void __launch_bounds__(kAltThreads, 1)
     *reinterpret_cast<uint4*>(smem + L::kOffV + s * L::kV + (D + r) * 128 + c * 16) = make_uint4(fill, fill, fill, fill);
   }
   if constexpr (BV) {
-    // zero the FP16 operands once: per tile only the first K pair of a row changes
-    for (int i = threadIdx.x; i < (128 * 32 + kVS * L::kMean) / 16; i += kAltThreads)
-      *reinterpret_cast<uint4*>(smem + L::kOffMassA + i * 16) = make_uint4(0, 0, 0, 0);
+    // zero the pending masses and the FP16 operands once
+    for (int i = threadIdx.x; i < (2 * 128 * 16 + 128 * 32 + 2 * L::kMean) / 16; i += kAltThreads)
+      *reinterpret_cast<uint4*>(smem + L::kOffPend + i * 16) = make_uint4(0, 0, 0, 0);
   }
   fence_proxy_async_smem();
   if (warp == 9) {
@@ -182,27 +201,33 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       }
     } else if (warp == 10 && BV) {
       // ------------------------------------- V producer + means operand (warp)
-      // lane l writes channels [l*D/32, (l+1)*D/32) of the tile's means
-      constexpr int CPL = D / 32;
+      // lane l writes channels l, l+32, ... of tile j's means into slot j%8
+      // of batch buffer (j/8)%2.  Buffer k%2 is written again for batch k+2
+      // only after PV(8k+13) has completed (the v_empty wait below), and the
+      // MMA of batch k precedes PV(8k+8), so no other release is needed.
       for (int j = 0; j < T; ++j) {
         const int s = j % kVS;
-        if (j >= kVS) {
-          if (!mbar_wait_warp(&bar->v_empty[s], ((j / kVS) & 1) ^ 1, kErrTimeoutProducer)) break;
-          if (!mbar_wait_warp(&bar->mean_empty[s], ((j / kVS) & 1) ^ 1, kErrTimeoutProducer)) break;
-        }
+        if (j >= kVS && !mbar_wait_warp(&bar->v_empty[s], ((j / kVS) & 1) ^ 1, kErrTimeoutProducer)) break;
         if (lane == 0) {
           mbar_expect_tx(&bar->v_full[s], D * 128);
           tma_load_3d(smem + L::kOffV + s * L::kV, &tmv, &bar->v_full[s], j * 128, 0, static_cast<int>(bh));
         }
-        const uint16_t* mrow = reinterpret_cast<const uint16_t*>(p.means) + (bh * T + j) * D + lane * CPL;
-        uint8_t* mop = smem + L::kOffMean + s * L::kMean;
+        const int kb = j >> 3, slot = j & 7;
+        const uint16_t* mrow = reinterpret_cast<const uint16_t*>(p.means) + (bh * T + j) * D;
+        uint8_t* mop = smem + L::kOffMean + (kb & 1) * L::kMean;
 #pragma unroll
-        for (int c = 0; c < CPL; ++c) {
+        for (int cc = 0; cc < D / 32; ++cc) {
+          const int c = lane + 32 * cc;
           const uint32_t m16 = __ldg(mrow + c);
-          *reinterpret_cast<uint32_t*>(mop + plain32_offset(lane * CPL + c)) = m16 | (m16 << 16);
+          *reinterpret_cast<uint32_t*>(mop + plain32_offset(c) + (slot >> 2) * 128 + (slot & 3) * 4) = m16 | (m16 << 16);
+          if (j == T - 1)   // the final batch's unused slots: zeros (their A entries are zero too)
+            for (int z = slot + 1; z < 8; ++z)
+              *reinterpret_cast<uint32_t*>(mop + plain32_offset(c) + (z >> 2) * 128 + (z & 3) * 4) = 0u;
         }
-        fence_proxy_async_smem();
-        mbar_arrive(&bar->mean_full[s]);
+        if (slot == 7 || j == T - 1) {
+          fence_proxy_async_smem();
+          mbar_arrive(&bar->mean_full[kb & 1]);
+        }
       }
     } else if (warp == 9 && lane == 0) {
       // ------------------------------------------------------- QK^T issuer
@@ -241,17 +266,16 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       bool ok = true;
       for (int j = 0; j < T && ok; ++j) {
         const int s = j % kVS, b = j & 1;
+        const int kb = (j >> 3) - 1;   // block means: batch kb completes at tile j = 8kb + 8
         ok = mbar_wait(&bar->p_full[b], (j >> 1) & 1, kErrTimeoutMma) &&
              mbar_wait(&bar->v_full[s], (j / kVS) & 1, kErrTimeoutMma);
-        if (BV && ok && j >= 1)
-          ok = mbar_wait(&bar->mean_full[(j - 1) % kVS], ((j - 1) / kVS) & 1, kErrTimeoutMma);
+        if (BV && ok && j >= 8 && (j & 7) == 0)
+          ok = mbar_wait(&bar->mean_full[kb & 1], (kb >> 1) & 1, kErrTimeoutMma);
         if (!ok) break;
         tc_fence_after();
         if constexpr (BV) {
-          if (j >= 1) {   // O += (mass_{j-1} alpha_j) x mean_{j-1}, written by the group of tile j
-            mma_f16_ss(tmem + kAColO, massdesc, meandesc0 + ((j - 1) % kVS) * kStepMean, idesc_mean, 1u);
-            mma_commit(&bar->mean_empty[(j - 1) % kVS]);
-          }
+          if (j >= 8 && (j & 7) == 0)   // O += sum over the batch of (mass alpha...) x mean
+            mma_f16_ss(tmem + kAColO, massdesc, meandesc0 + (kb & 1) * kStepMean, idesc_mean, 1u);
         }
         const uint64_t vd = vdesc0 + s * kStepV;
         const uint32_t pcol = tmem + (b ? kAColP1 : kAColP0);
@@ -262,13 +286,13 @@ __global__ void __launch_bounds__(kAltThreads, 1)
         mma_commit(&bar->pv_done[(j + 1) & 1]);
       }
       if constexpr (BV) {
-        // the last tile's means: mass_{T-1} comes from the group of parity T%2
+        // the final batch: its A operand comes from the group of parity T%2
+        const int kb = (T - 1) >> 3;
         if (ok) ok = mbar_wait(&bar->p_full[T & 1], (T >> 1) & 1, kErrTimeoutMma) &&
-                     mbar_wait(&bar->mean_full[(T - 1) % kVS], ((T - 1) / kVS) & 1, kErrTimeoutMma);
+                     mbar_wait(&bar->mean_full[kb & 1], (kb >> 1) & 1, kErrTimeoutMma);
         if (ok) {
           tc_fence_after();
-          mma_f16_ss(tmem + kAColO, massdesc, meandesc0 + ((T - 1) % kVS) * kStepMean, idesc_mean, 1u);
-          mma_commit(&bar->mean_empty[(T - 1) % kVS]);
+          mma_f16_ss(tmem + kAColO, massdesc, meandesc0 + (kb & 1) * kStepMean, idesc_mean, 1u);
         }
       }
       if (ok) mma_commit(&bar->o_final);
@@ -417,7 +441,8 @@ __global__ void __launch_bounds__(kAltThreads, 1)
         }
       }
       // rescale O (and the denominator column) between PV(j-1) and PV(j) if any max grew
-      if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+      const bool grew = j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f);
+      if (grew) {
         tc_fence_after();
         const uint32_t ocol = tmem + lane_base + kAColO;
         const uint64_t alpha2 = pk2f(alpha, alpha);
@@ -440,15 +465,23 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       }
       if constexpr (BV) {
         float* dbuf = reinterpret_cast<float*>(smem + L::kOffD);
-        if (j >= 1) {   // mass_{j-1} alpha_j as FP16 hi + lo: row t of the means MMA's A operand
+        if (j >= 1) {   // pending masses to O's scale at PV(j); mass_{j-1} alpha_j into slot (j-1)%8
           ok = mbar_wait_warp(&bar->d_ready[b ^ 1][quarter], ((j - 1) >> 1) & 1, kErrTimeoutSoftmax);
           if (!ok) break;
-          const float ms = __fmul_rn(__fsub_rn(dcur, dbuf[(b ^ 1) * 128 + t]), alpha);
-          const __half hi = __float2half_rn(ms);
-          const __half lo = __float2half_rn(__fsub_rn(ms, __half2float(hi)));
-          *reinterpret_cast<uint32_t*>(smem + L::kOffMassA + plain32_offset(t)) =
-              static_cast<uint32_t>(__half_as_ushort(hi)) | (static_cast<uint32_t>(__half_as_ushort(lo)) << 16);
-          fence_proxy_async_smem();
+          float4* pend = reinterpret_cast<float4*>(smem + L::kOffPend);
+          if (grew) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              float4 v = pend[h * 128 + t];
+              v.x = __fmul_rn(v.x, alpha); v.y = __fmul_rn(v.y, alpha);
+              v.z = __fmul_rn(v.z, alpha); v.w = __fmul_rn(v.w, alpha);
+              pend[h * 128 + t] = v;
+            }
+          }
+          const int slot = (j - 1) & 7;
+          reinterpret_cast<float*>(pend + (slot >> 2) * 128 + t)[slot & 3] =
+              __fmul_rn(__fsub_rn(dcur, dbuf[(b ^ 1) * 128 + t]), alpha);
+          if (slot == 7) write_mass_operand(smem + L::kOffMassA, pend, t, 8);
         }
         // the denominator column just before PV(j), for the group of tile j+1
         dbuf[b * 128 + t] = j >= 1 ? __fmul_rn(dcur, alpha) : 0.f;
@@ -470,12 +503,11 @@ __global__ void __launch_bounds__(kAltThreads, 1)
           tc_fence_after();
           const float dlast = __uint_as_float(tmem_ld1(tmem + lane_base + kAColO + D));
           tmem_wait_ld();
-          const float ms = __fsub_rn(dlast, reinterpret_cast<const float*>(smem + L::kOffD)[((T - 1) & 1) * 128 + t]);
-          const __half hi = __float2half_rn(ms);
-          const __half lo = __float2half_rn(__fsub_rn(ms, __half2float(hi)));
-          *reinterpret_cast<uint32_t*>(smem + L::kOffMassA + plain32_offset(t)) =
-              static_cast<uint32_t>(__half_as_ushort(hi)) | (static_cast<uint32_t>(__half_as_ushort(lo)) << 16);
-          fence_proxy_async_smem();
+          float4* pend = reinterpret_cast<float4*>(smem + L::kOffPend);
+          const int slot = (T - 1) & 7;
+          reinterpret_cast<float*>(pend + (slot >> 2) * 128 + t)[slot & 3] =
+              __fsub_rn(dlast, reinterpret_cast<const float*>(smem + L::kOffD)[((T - 1) & 1) * 128 + t]);
+          write_mass_operand(smem + L::kOffMassA, pend, t, slot + 1);
           tc_fence_before();
           mbar_arrive(&bar->p_full[T & 1]);
         }
