@@ -42,12 +42,16 @@
 // lo_7], the FP16 hi + lo split (exact to ~2^-22) of the batch's 8 masses,
 // and channel c of the Dx16 B operand holds [mean_0, mean_0, ..., mean_7,
 // mean_7] (written by the V producer warp, two batch buffers).  Until its
-// batch is applied a mass waits in FP32 in shared memory at O's scale: the
-// group of tile j multiplies the pending masses by alpha_j as it rescales O.
-// The group of tile 8k+8 completes batch k (mass_{8k+7}), writes the A
-// operand, and the batch's MMA goes just before PV(8k+8); after the last
-// tile the group of parity T%2 completes the final, possibly partial, batch
-// (its unused slots zero) and that MMA precedes o_final.
+// batch is applied a mass waits in FP32 in shared memory at O's scale.
+// Everything between PV(j-1) completing and P(j) being released is on the
+// critical chain of the kernel, so the mass bookkeeping of tile j (mass_{j-1},
+// the pending masses times alpha_j, the handover) runs after P(j) is
+// released; only the read of the denominator column stays before it.  Batch k
+// is therefore complete after tile 8k+8's bookkeeping, and the group of tile
+// 8k+9 writes its A operand (pending masses times alpha_{8k+9}) before
+// releasing P(8k+9); its MMA precedes PV(8k+9).  After the last tile the
+// group of parity T%2 completes the batches still open (one or two, the last
+// possibly partial with its unused slots zero) and their MMAs precede o_final.
 //
 // Barrier phases.  Every parity wait below is unconditional (taken on every
 // tile), so a waiter can never be two phases behind its barrier, and no
@@ -89,10 +93,11 @@ struct AltSmem {
   // block means: FP16 operands without swizzle, rows of 32 bytes (K = 16),
   // 8-row groups 256 bytes apart, the two K halves 128 bytes apart
   static constexpr int kOffD = kOffM + 2 * 128 * 4;        // float [2][128] denominators before PV(j)
-  static constexpr int kOffPend = kOffD + 2 * 128 * 4;     // float4 [2][128]: row t's 8 pending masses
-  static constexpr int kOffMassA = kOffPend + 2 * 128 * 16;  // 128 x 16 FP16 (mass hi, lo) x 8 tiles
+  static constexpr int kOffPend = kOffD + 2 * 128 * 4;     // float4 [4][128]: row t's masses, slot j%16
+  static constexpr int kMassA = 128 * 32;                    // 128 x 16 FP16 (mass hi, lo) x 8 tiles
+  static constexpr int kOffMassA = kOffPend + 4 * 128 * 16;  // two batch buffers
   static constexpr int kMean = D * 32;                       // D x 16 FP16 (mean, mean) x 8 tiles
-  static constexpr int kOffMean = kOffMassA + 128 * 32;      // two batch buffers
+  static constexpr int kOffMean = kOffMassA + 2 * kMassA;    // two batch buffers
   static constexpr int kOffBar = kOffMean + 2 * kMean;
   static constexpr int kOffSlot = kOffBar + int(sizeof(AltBarriers));
   static constexpr int kBytes = kOffSlot + 16;
@@ -102,21 +107,22 @@ struct AltSmem {
 // Byte offset of (row, first K element) in the no-swizzle 32-byte-row layout.
 __device__ __forceinline__ int plain32_offset(int r) { return (r >> 3) * 256 + (r & 7) * 16; }
 
-// Row t of the means MMA's A operand from row t's pending masses: the first
-// n as FP16 hi + lo pairs, the rest zero; then made visible to the MMA.
-__device__ __forceinline__ void write_mass_operand(uint8_t* a, const float4* pend, int t, int n) {
-  const float4 x0 = pend[t], x1 = pend[128 + t];
-  const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+// Row t of a means MMA's A operand from the pending masses of batch parity h
+// times sc: the first n as FP16 hi + lo pairs, the rest zero.  The caller
+// makes the stores visible to the MMA (fence.proxy.async).
+__device__ __forceinline__ void write_mass_operand(uint8_t* a, const float4* pend, int h, int t, int n, float sc) {
+  const float4 x0 = pend[(2 * h) * 128 + t], x1 = pend[(2 * h + 1) * 128 + t];
+  const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
   uint32_t wd[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const __half hi = __float2half_rn(x[i]);
-    const __half lo = __float2half_rn(__fsub_rn(x[i], __half2float(hi)));
+    const float x = __fmul_rn(xs[i], sc);
+    const __half hi = __float2half_rn(x);
+    const __half lo = __float2half_rn(__fsub_rn(x, __half2float(hi)));
     wd[i] = i < n ? static_cast<uint32_t>(__half_as_ushort(hi)) | (static_cast<uint32_t>(__half_as_ushort(lo)) << 16) : 0u;
   }
   *reinterpret_cast<uint4*>(a + plain32_offset(t)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
   *reinterpret_cast<uint4*>(a + plain32_offset(t) + 128) = make_uint4(wd[4], wd[5], wd[6], wd[7]);
-  fence_proxy_async_smem();
 }
 
 template <int D, typename OutT, bool BV>
@@ -166,7 +172,7 @@ __global__ void __launch_bounds__(kAltThreads, 1)
   }
   if constexpr (BV) {
     // zero the pending masses and the FP16 operands once
-    for (int i = threadIdx.x; i < (2 * 128 * 16 + 128 * 32 + 2 * L::kMean) / 16; i += kAltThreads)
+    for (int i = threadIdx.x; i < (4 * 128 * 16 + 2 * L::kMassA + 2 * L::kMean) / 16; i += kAltThreads)
       *reinterpret_cast<uint4*>(smem + L::kOffPend + i * 16) = make_uint4(0, 0, 0, 0);
   }
   fence_proxy_async_smem();
@@ -205,6 +211,11 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       // of batch buffer (j/8)%2.  Buffer k%2 is written again for batch k+2
       // only after PV(8k+13) has completed (the v_empty wait below), and the
       // MMA of batch k precedes PV(8k+8), so no other release is needed.
+      // Tile j+1's means are loaded while the warp waits for tile j+1's V slot.
+      const uint16_t* mbase = reinterpret_cast<const uint16_t*>(p.means) + bh * T * D;
+      uint32_t mnext[D / 32];
+#pragma unroll
+      for (int cc = 0; cc < D / 32; ++cc) mnext[cc] = __ldg(mbase + lane + 32 * cc);
       for (int j = 0; j < T; ++j) {
         const int s = j % kVS;
         if (j >= kVS && !mbar_wait_warp(&bar->v_empty[s], ((j / kVS) & 1) ^ 1, kErrTimeoutProducer)) break;
@@ -212,13 +223,18 @@ __global__ void __launch_bounds__(kAltThreads, 1)
           mbar_expect_tx(&bar->v_full[s], D * 128);
           tma_load_3d(smem + L::kOffV + s * L::kV, &tmv, &bar->v_full[s], j * 128, 0, static_cast<int>(bh));
         }
+        uint32_t mcur[D / 32];
+#pragma unroll
+        for (int cc = 0; cc < D / 32; ++cc) {
+          mcur[cc] = mnext[cc];
+          if (j + 1 < T) mnext[cc] = __ldg(mbase + (j + 1) * D + lane + 32 * cc);
+        }
         const int kb = j >> 3, slot = j & 7;
-        const uint16_t* mrow = reinterpret_cast<const uint16_t*>(p.means) + (bh * T + j) * D;
         uint8_t* mop = smem + L::kOffMean + (kb & 1) * L::kMean;
 #pragma unroll
         for (int cc = 0; cc < D / 32; ++cc) {
           const int c = lane + 32 * cc;
-          const uint32_t m16 = __ldg(mrow + c);
+          const uint32_t m16 = mcur[cc];
           *reinterpret_cast<uint32_t*>(mop + plain32_offset(c) + (slot >> 2) * 128 + (slot & 3) * 4) = m16 | (m16 << 16);
           if (j == T - 1)   // the final batch's unused slots: zeros (their A entries are zero too)
             for (int z = slot + 1; z < 8; ++z)
@@ -260,23 +276,23 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       constexpr uint32_t idesc_mean = idesc_make(1, 0, 0, 128, D);     // f32 <- f16 x f16
       const uint64_t vdesc0 = smem_desc_sw128(smem_u32(smem + L::kOffV));
       constexpr uint64_t kStepV = (L::kV >> 4);
-      const uint64_t massdesc = smem_desc_plain(smem_u32(smem + L::kOffMassA), 128, 256);
+      const uint64_t massdesc0 = smem_desc_plain(smem_u32(smem + L::kOffMassA), 128, 256);
+      constexpr uint64_t kStepMassA = (L::kMassA >> 4);
       const uint64_t meandesc0 = smem_desc_plain(smem_u32(smem + L::kOffMean), 128, 256);
       constexpr uint64_t kStepMean = (L::kMean >> 4);
       bool ok = true;
       for (int j = 0; j < T && ok; ++j) {
         const int s = j % kVS, b = j & 1;
-        const int kb = (j >> 3) - 1;   // block means: batch kb completes at tile j = 8kb + 8
+        const bool mean_mma = BV && j >= 9 && ((j - 9) & 7) == 0;   // batch kb goes before PV(8kb+9)
+        const int kb = (j - 9) >> 3;
         ok = mbar_wait(&bar->p_full[b], (j >> 1) & 1, kErrTimeoutMma) &&
              mbar_wait(&bar->v_full[s], (j / kVS) & 1, kErrTimeoutMma);
-        if (BV && ok && j >= 8 && (j & 7) == 0)
-          ok = mbar_wait(&bar->mean_full[kb & 1], (kb >> 1) & 1, kErrTimeoutMma);
+        if (ok && mean_mma) ok = mbar_wait(&bar->mean_full[kb & 1], (kb >> 1) & 1, kErrTimeoutMma);
         if (!ok) break;
         tc_fence_after();
-        if constexpr (BV) {
-          if (j >= 8 && (j & 7) == 0)   // O += sum over the batch of (mass alpha...) x mean
-            mma_f16_ss(tmem + kAColO, massdesc, meandesc0 + (kb & 1) * kStepMean, idesc_mean, 1u);
-        }
+        if (mean_mma)   // O += sum over the batch's tiles of (mass alpha...) x mean
+          mma_f16_ss(tmem + kAColO, massdesc0 + (kb & 1) * kStepMassA, meandesc0 + (kb & 1) * kStepMean,
+                     idesc_mean, 1u);
         const uint64_t vd = vdesc0 + s * kStepV;
         const uint32_t pcol = tmem + (b ? kAColP1 : kAColP0);
 #pragma unroll
@@ -286,13 +302,16 @@ __global__ void __launch_bounds__(kAltThreads, 1)
         mma_commit(&bar->pv_done[(j + 1) & 1]);
       }
       if constexpr (BV) {
-        // the final batch: its A operand comes from the group of parity T%2
-        const int kb = (T - 1) >> 3;
-        if (ok) ok = mbar_wait(&bar->p_full[T & 1], (T >> 1) & 1, kErrTimeoutMma) &&
-                     mbar_wait(&bar->mean_full[kb & 1], (kb >> 1) & 1, kErrTimeoutMma);
-        if (ok) {
+        // the open batches: their A operands come from the group of parity T%2
+        const int kl = (T - 1) >> 3;
+        const int kf = (((T - 1) & 7) == 0 && kl >= 1) ? kl - 1 : kl;
+        if (ok) ok = mbar_wait(&bar->p_full[T & 1], (T >> 1) & 1, kErrTimeoutMma);
+        for (int kb = kf; kb <= kl && ok; ++kb) {
+          ok = mbar_wait(&bar->mean_full[kb & 1], (kb >> 1) & 1, kErrTimeoutMma);
+          if (!ok) break;
           tc_fence_after();
-          mma_f16_ss(tmem + kAColO, massdesc, meandesc0 + (kb & 1) * kStepMean, idesc_mean, 1u);
+          mma_f16_ss(tmem + kAColO, massdesc0 + (kb & 1) * kStepMassA, meandesc0 + (kb & 1) * kStepMean,
+                     idesc_mean, 1u);
         }
       }
       if (ok) mma_commit(&bar->o_final);
@@ -430,14 +449,13 @@ __global__ void __launch_bounds__(kAltThreads, 1)
         }
       }
       // PV(j-1) complete (hence PV(j-2) too): P[b] is free and O may be rescaled
-      float dcur = 0.f;   // block means: denominator column after PV(j-1)
+      uint32_t draw = 0;   // block means: denominator column after PV(j-1), read before P(j) is released
       if (j >= 1) {
         ok = mbar_wait_warp(&bar->pv_done[b], ((j - 1) >> 1) & 1, kErrTimeoutSoftmax);
         if (!ok) break;
         if constexpr (BV) {
           tc_fence_after();
-          dcur = __uint_as_float(tmem_ld1(tmem + lane_base + kAColO + D));
-          tmem_wait_ld();
+          draw = tmem_ld1(tmem + lane_base + kAColO + D);
         }
       }
       // rescale O (and the denominator column) between PV(j-1) and PV(j) if any max grew
@@ -456,46 +474,56 @@ __global__ void __launch_bounds__(kAltThreads, 1)
           tmem_st32(ocol + cc * 32, o);
         }
         // the denominator: column D (columns D+1.. of the block only ever hold zeros)
-        float dn = dcur;
-        if constexpr (!BV) {
-          dn = __uint_as_float(tmem_ld1(ocol + D));
-          tmem_wait_ld();
-        }
-        tmem_st1(ocol + D, __float_as_uint(__fmul_rn(dn, alpha)));
+        if constexpr (!BV) draw = tmem_ld1(ocol + D);
+        tmem_wait_ld_reg(draw);
+        tmem_st1(ocol + D, __float_as_uint(__fmul_rn(__uint_as_float(draw), alpha)));
       }
-      if constexpr (BV) {
-        float* dbuf = reinterpret_cast<float*>(smem + L::kOffD);
-        if (j >= 1) {   // pending masses to O's scale at PV(j); mass_{j-1} alpha_j into slot (j-1)%8
-          ok = mbar_wait_warp(&bar->d_ready[b ^ 1][quarter], ((j - 1) >> 1) & 1, kErrTimeoutSoftmax);
-          if (!ok) break;
-          float4* pend = reinterpret_cast<float4*>(smem + L::kOffPend);
-          if (grew) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              float4 v = pend[h * 128 + t];
-              v.x = __fmul_rn(v.x, alpha); v.y = __fmul_rn(v.y, alpha);
-              v.z = __fmul_rn(v.z, alpha); v.w = __fmul_rn(v.w, alpha);
-              pend[h * 128 + t] = v;
-            }
-          }
-          const int slot = (j - 1) & 7;
-          reinterpret_cast<float*>(pend + (slot >> 2) * 128 + t)[slot & 3] =
-              __fmul_rn(__fsub_rn(dcur, dbuf[(b ^ 1) * 128 + t]), alpha);
-          if (slot == 7) write_mass_operand(smem + L::kOffMassA, pend, t, 8);
-        }
-        // the denominator column just before PV(j), for the group of tile j+1
-        dbuf[b * 128 + t] = j >= 1 ? __fmul_rn(dcur, alpha) : 0.f;
-        mbar_arrive(&bar->d_ready[b][quarter]);
+      float4* pend = reinterpret_cast<float4*>(smem + L::kOffPend);
+      float* dbuf = reinterpret_cast<float*>(smem + L::kOffD);
+      if (BV && j >= 9 && ((j - 9) & 7) == 0) {
+        // batch (j-9)/8 is complete once tile j-1's bookkeeping is: its A
+        // operand at O's scale for PV(j), before P(j) is released
+        ok = mbar_wait_warp(&bar->d_ready[b ^ 1][quarter], ((j - 1) >> 1) & 1, kErrTimeoutSoftmax);
+        if (!ok) break;
+        const int kb = (j - 9) >> 3;
+        write_mass_operand(smem + L::kOffMassA + (kb & 1) * L::kMassA, pend, kb & 1, t, 8, alpha);
+        fence_proxy_async_smem();
       }
       // P(j) into this group's P buffer (PV(j-2) has consumed it, see above)
       tc_fence_after();
       tmem_st32(tmem + lane_base + (b ? kAColP1 : kAColP0), pw);
       tmem_wait_st();
+      if constexpr (BV) tmem_wait_ld_reg(draw);   // the column read completes before PV(j) may start
       tc_fence_before();
       mbar_arrive(&bar->p_full[b]);
+      if constexpr (BV) {
+        // bookkeeping off the critical chain: mass_{j-1} alpha_j into slot (j-1)%16,
+        // the open batch's pending masses times alpha_j, the handover to tile j+1
+        const float dcur = __uint_as_float(draw);
+        if (j >= 1) {
+          ok = mbar_wait_warp(&bar->d_ready[b ^ 1][quarter], ((j - 1) >> 1) & 1, kErrTimeoutSoftmax);
+          if (!ok) break;
+          const int slot = (j - 1) & 15;
+          if (grew) {
+            const int h = slot >> 3;
+#pragma unroll
+            for (int q4 = 0; q4 < 2; ++q4) {
+              float4 v = pend[(2 * h + q4) * 128 + t];
+              v.x = __fmul_rn(v.x, alpha); v.y = __fmul_rn(v.y, alpha);
+              v.z = __fmul_rn(v.z, alpha); v.w = __fmul_rn(v.w, alpha);
+              pend[(2 * h + q4) * 128 + t] = v;
+            }
+          }
+          reinterpret_cast<float*>(pend + (slot >> 2) * 128 + t)[slot & 3] =
+              __fmul_rn(__fsub_rn(dcur, dbuf[(b ^ 1) * 128 + t]), alpha);
+        }
+        // the denominator column just before PV(j), for the group of tile j+1
+        dbuf[b * 128 + t] = j >= 1 ? __fmul_rn(dcur, alpha) : 0.f;
+        mbar_arrive(&bar->d_ready[b][quarter]);
+      }
     }
     if constexpr (BV) {
-      // the group of parity T%2 hands over mass_{T-1} for the last means MMA
+      // the group of parity T%2 completes the open batches for the last means MMAs
       if (ok && (T & 1) == w) {
         ok = mbar_wait_warp(&bar->pv_done[T & 1], ((T - 1) >> 1) & 1, kErrTimeoutSoftmax) &&
              mbar_wait_warp(&bar->d_ready[(T - 1) & 1][quarter], ((T - 1) >> 1) & 1, kErrTimeoutSoftmax);
@@ -504,10 +532,15 @@ __global__ void __launch_bounds__(kAltThreads, 1)
           const float dlast = __uint_as_float(tmem_ld1(tmem + lane_base + kAColO + D));
           tmem_wait_ld();
           float4* pend = reinterpret_cast<float4*>(smem + L::kOffPend);
-          const int slot = (T - 1) & 7;
+          const int slot = (T - 1) & 15;
           reinterpret_cast<float*>(pend + (slot >> 2) * 128 + t)[slot & 3] =
               __fsub_rn(dlast, reinterpret_cast<const float*>(smem + L::kOffD)[((T - 1) & 1) * 128 + t]);
-          write_mass_operand(smem + L::kOffMassA, pend, t, slot + 1);
+          const int kl = (T - 1) >> 3;
+          const int kf = (((T - 1) & 7) == 0 && kl >= 1) ? kl - 1 : kl;
+          for (int kb = kf; kb <= kl; ++kb)
+            write_mass_operand(smem + L::kOffMassA + (kb & 1) * L::kMassA, pend, kb & 1, t,
+                               kb < kl ? 8 : ((T - 1) & 7) + 1, 1.f);
+          fence_proxy_async_smem();
           tc_fence_before();
           mbar_arrive(&bar->p_full[T & 1]);
         }

@@ -298,6 +298,10 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// wait::ld that also ties register r to the wait, so no use of r is scheduled before it
+__device__ __forceinline__ void tmem_wait_ld_reg(uint32_t& r) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(r) :: "memory");
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // 32 lanes x 32 bit, 32 consecutive columns per thread.
