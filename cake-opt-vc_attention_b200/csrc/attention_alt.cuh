@@ -46,12 +46,13 @@
 // Everything between PV(j-1) completing and P(j) being released is on the
 // critical chain of the kernel, so the mass bookkeeping of tile j (mass_{j-1},
 // the pending masses times alpha_j, the handover) runs after P(j) is
-// released; only the read of the denominator column stays before it.  Batch k
-// is therefore complete after tile 8k+8's bookkeeping, and the group of tile
-// 8k+9 writes its A operand (pending masses times alpha_{8k+9}) before
-// releasing P(8k+9); its MMA precedes PV(8k+9).  After the last tile the
-// group of parity T%2 completes the batches still open (one or two, the last
-// possibly partial with its unused slots zero) and their MMAs precede o_final.
+// released, while PV(j) executes; only the read of the denominator column
+// stays before it.  Batch k is complete after tile 8k+8's bookkeeping, which
+// also writes the batch's A operand (its masses are at O's scale for PV(8k+8))
+// and arrives on a_full; the P.V issuer issues the batch's MMA right after
+// PV(8k+8) and commits pv_done after it, so the next rescale of O follows it.
+// After the last tile the group of parity T%2 completes the open batch
+// (possibly partial, its unused slots zero) and that MMA precedes o_final.
 //
 // Barrier phases.  Every parity wait below is unconditional (taken on every
 // tile), so a waiter can never be two phases behind its barrier, and no
@@ -80,6 +81,7 @@ struct __align__(8) AltBarriers {
   uint64_t pv_done[2];      // PV(i) completes pv_done[(i+1)&1]: the group of tile i+1 waits on it
   uint64_t m_ready[2][4];   // [tile parity][warp of the group]
   uint64_t mean_full[2];                      // block means: batch buffer k%2 of the means operand written
+  uint64_t a_full;                            // block means: a batch's A operand written (count 128)
   uint64_t d_ready[2][4];                     // block means: denominator before PV(j) handed over
 };
 
@@ -93,11 +95,11 @@ struct AltSmem {
   // block means: FP16 operands without swizzle, rows of 32 bytes (K = 16),
   // 8-row groups 256 bytes apart, the two K halves 128 bytes apart
   static constexpr int kOffD = kOffM + 2 * 128 * 4;        // float [2][128] denominators before PV(j)
-  static constexpr int kOffPend = kOffD + 2 * 128 * 4;     // float4 [4][128]: row t's masses, slot j%16
+  static constexpr int kOffPend = kOffD + 2 * 128 * 4;     // float4 [2][128]: row t's masses, slot j%8
   static constexpr int kMassA = 128 * 32;                    // 128 x 16 FP16 (mass hi, lo) x 8 tiles
-  static constexpr int kOffMassA = kOffPend + 4 * 128 * 16;  // two batch buffers
+  static constexpr int kOffMassA = kOffPend + 2 * 128 * 16;
   static constexpr int kMean = D * 32;                       // D x 16 FP16 (mean, mean) x 8 tiles
-  static constexpr int kOffMean = kOffMassA + 2 * kMassA;    // two batch buffers
+  static constexpr int kOffMean = kOffMassA + kMassA;        // two batch buffers
   static constexpr int kOffBar = kOffMean + 2 * kMean;
   static constexpr int kOffSlot = kOffBar + int(sizeof(AltBarriers));
   static constexpr int kBytes = kOffSlot + 16;
@@ -107,22 +109,23 @@ struct AltSmem {
 // Byte offset of (row, first K element) in the no-swizzle 32-byte-row layout.
 __device__ __forceinline__ int plain32_offset(int r) { return (r >> 3) * 256 + (r & 7) * 16; }
 
-// Row t of a means MMA's A operand from the pending masses of batch parity h
-// times sc: the first n as FP16 hi + lo pairs, the rest zero.  The caller
-// makes the stores visible to the MMA (fence.proxy.async).
-__device__ __forceinline__ void write_mass_operand(uint8_t* a, const float4* pend, int h, int t, int n, float sc) {
-  const float4 x0 = pend[(2 * h) * 128 + t], x1 = pend[(2 * h + 1) * 128 + t];
-  const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+// Row t of the means MMA's A operand from row t's 8 pending masses: the first
+// n as FP16 hi + lo pairs, the rest zero; then made visible to the MMA.
+__device__ __forceinline__ void write_mass_operand(uint8_t* a, const float4* pend, int t, int n) {
+  const float4 x0 = pend[t], x1 = pend[128 + t];
+  const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
   uint32_t wd[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float x = __fmul_rn(xs[i], sc);
-    const __half hi = __float2half_rn(x);
-    const __half lo = __float2half_rn(__fsub_rn(x, __half2float(hi)));
-    wd[i] = i < n ? static_cast<uint32_t>(__half_as_ushort(hi)) | (static_cast<uint32_t>(__half_as_ushort(lo)) << 16) : 0u;
+  for (int i = 0; i < 8; i += 2) {
+    const __half2 hi = __floats2half2_rn(x[i], x[i + 1]);
+    const __half2 lo = __floats2half2_rn(__fsub_rn(x[i], __low2float(hi)), __fsub_rn(x[i + 1], __high2float(hi)));
+    const uint32_t h = *reinterpret_cast<const uint32_t*>(&hi), l = *reinterpret_cast<const uint32_t*>(&lo);
+    wd[i] = i < n ? __byte_perm(h, l, 0x5410) : 0u;           // [hi_i, lo_i]
+    wd[i + 1] = i + 1 < n ? __byte_perm(h, l, 0x7632) : 0u;   // [hi_i+1, lo_i+1]
   }
   *reinterpret_cast<uint4*>(a + plain32_offset(t)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
   *reinterpret_cast<uint4*>(a + plain32_offset(t) + 128) = make_uint4(wd[4], wd[5], wd[6], wd[7]);
+  fence_proxy_async_smem();
 }
 
 template <int D, typename OutT, bool BV>
@@ -160,6 +163,7 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       for (int q = 0; q < 4; ++q) mbar_init(&bar->m_ready[b][q], 32);
     }
     for (int s = 0; s < 2; ++s) mbar_init(&bar->mean_full[s], 32);
+    mbar_init(&bar->a_full, 128);
     for (int b = 0; b < 2; ++b)
       for (int q = 0; q < 4; ++q) mbar_init(&bar->d_ready[b][q], 32);
     mbar_init(&bar->o_final, 1);
@@ -172,7 +176,7 @@ __global__ void __launch_bounds__(kAltThreads, 1)
   }
   if constexpr (BV) {
     // zero the pending masses and the FP16 operands once
-    for (int i = threadIdx.x; i < (4 * 128 * 16 + 2 * L::kMassA + 2 * L::kMean) / 16; i += kAltThreads)
+    for (int i = threadIdx.x; i < (2 * 128 * 16 + L::kMassA + 2 * L::kMean) / 16; i += kAltThreads)
       *reinterpret_cast<uint4*>(smem + L::kOffPend + i * 16) = make_uint4(0, 0, 0, 0);
   }
   fence_proxy_async_smem();
@@ -276,42 +280,42 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       constexpr uint32_t idesc_mean = idesc_make(1, 0, 0, 128, D);     // f32 <- f16 x f16
       const uint64_t vdesc0 = smem_desc_sw128(smem_u32(smem + L::kOffV));
       constexpr uint64_t kStepV = (L::kV >> 4);
-      const uint64_t massdesc0 = smem_desc_plain(smem_u32(smem + L::kOffMassA), 128, 256);
-      constexpr uint64_t kStepMassA = (L::kMassA >> 4);
+      const uint64_t massdesc = smem_desc_plain(smem_u32(smem + L::kOffMassA), 128, 256);
       const uint64_t meandesc0 = smem_desc_plain(smem_u32(smem + L::kOffMean), 128, 256);
       constexpr uint64_t kStepMean = (L::kMean >> 4);
       bool ok = true;
       for (int j = 0; j < T && ok; ++j) {
         const int s = j % kVS, b = j & 1;
-        const bool mean_mma = BV && j >= 9 && ((j - 9) & 7) == 0;   // batch kb goes before PV(8kb+9)
-        const int kb = (j - 9) >> 3;
         ok = mbar_wait(&bar->p_full[b], (j >> 1) & 1, kErrTimeoutMma) &&
              mbar_wait(&bar->v_full[s], (j / kVS) & 1, kErrTimeoutMma);
-        if (ok && mean_mma) ok = mbar_wait(&bar->mean_full[kb & 1], (kb >> 1) & 1, kErrTimeoutMma);
         if (!ok) break;
         tc_fence_after();
-        if (mean_mma)   // O += sum over the batch's tiles of (mass alpha...) x mean
-          mma_f16_ss(tmem + kAColO, massdesc0 + (kb & 1) * kStepMassA, meandesc0 + (kb & 1) * kStepMean,
-                     idesc_mean, 1u);
         const uint64_t vd = vdesc0 + s * kStepV;
         const uint32_t pcol = tmem + (b ? kAColP1 : kAColP0);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           mma_f8_ts(tmem + kAColO, pcol + kk * 8, vd + 2 * kk, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&bar->v_empty[s]);
+        if (BV && j >= 8 && (j & 7) == 0) {
+          // batch kb, completed by tile j's bookkeeping while PV(j) runs:
+          // O += sum over the batch's tiles of (mass alpha...) x mean
+          const int kb = (j >> 3) - 1;
+          ok = mbar_wait(&bar->a_full, kb & 1, kErrTimeoutMma) &&
+               mbar_wait(&bar->mean_full[kb & 1], (kb >> 1) & 1, kErrTimeoutMma);
+          if (!ok) break;
+          tc_fence_after();
+          mma_f16_ss(tmem + kAColO, massdesc, meandesc0 + (kb & 1) * kStepMean, idesc_mean, 1u);
+        }
         mma_commit(&bar->pv_done[(j + 1) & 1]);
       }
       if constexpr (BV) {
-        // the open batches: their A operands come from the group of parity T%2
-        const int kl = (T - 1) >> 3;
-        const int kf = (((T - 1) & 7) == 0 && kl >= 1) ? kl - 1 : kl;
-        if (ok) ok = mbar_wait(&bar->p_full[T & 1], (T >> 1) & 1, kErrTimeoutMma);
-        for (int kb = kf; kb <= kl && ok; ++kb) {
-          ok = mbar_wait(&bar->mean_full[kb & 1], (kb >> 1) & 1, kErrTimeoutMma);
-          if (!ok) break;
+        // the open batch: its A operand comes from the group of parity T%2
+        const int kb = (T - 1) >> 3;
+        if (ok) ok = mbar_wait(&bar->p_full[T & 1], (T >> 1) & 1, kErrTimeoutMma) &&
+                     mbar_wait(&bar->mean_full[kb & 1], (kb >> 1) & 1, kErrTimeoutMma);
+        if (ok) {
           tc_fence_after();
-          mma_f16_ss(tmem + kAColO, massdesc0 + (kb & 1) * kStepMassA, meandesc0 + (kb & 1) * kStepMean,
-                     idesc_mean, 1u);
+          mma_f16_ss(tmem + kAColO, massdesc, meandesc0 + (kb & 1) * kStepMean, idesc_mean, 1u);
         }
       }
       if (ok) mma_commit(&bar->o_final);
@@ -480,15 +484,6 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       }
       float4* pend = reinterpret_cast<float4*>(smem + L::kOffPend);
       float* dbuf = reinterpret_cast<float*>(smem + L::kOffD);
-      if (BV && j >= 9 && ((j - 9) & 7) == 0) {
-        // batch (j-9)/8 is complete once tile j-1's bookkeeping is: its A
-        // operand at O's scale for PV(j), before P(j) is released
-        ok = mbar_wait_warp(&bar->d_ready[b ^ 1][quarter], ((j - 1) >> 1) & 1, kErrTimeoutSoftmax);
-        if (!ok) break;
-        const int kb = (j - 9) >> 3;
-        write_mass_operand(smem + L::kOffMassA + (kb & 1) * L::kMassA, pend, kb & 1, t, 8, alpha);
-        fence_proxy_async_smem();
-      }
       // P(j) into this group's P buffer (PV(j-2) has consumed it, see above)
       tc_fence_after();
       tmem_st32(tmem + lane_base + (b ? kAColP1 : kAColP0), pw);
@@ -497,25 +492,29 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       tc_fence_before();
       mbar_arrive(&bar->p_full[b]);
       if constexpr (BV) {
-        // bookkeeping off the critical chain: mass_{j-1} alpha_j into slot (j-1)%16,
-        // the open batch's pending masses times alpha_j, the handover to tile j+1
+        // bookkeeping off the critical chain, while PV(j) runs: the pending
+        // masses times alpha_j, mass_{j-1} alpha_j into slot (j-1)%8, the A
+        // operand when that completes a batch, the handover to tile j+1
         const float dcur = __uint_as_float(draw);
         if (j >= 1) {
           ok = mbar_wait_warp(&bar->d_ready[b ^ 1][quarter], ((j - 1) >> 1) & 1, kErrTimeoutSoftmax);
           if (!ok) break;
-          const int slot = (j - 1) & 15;
+          const int slot = (j - 1) & 7;
           if (grew) {
-            const int h = slot >> 3;
 #pragma unroll
-            for (int q4 = 0; q4 < 2; ++q4) {
-              float4 v = pend[(2 * h + q4) * 128 + t];
+            for (int h = 0; h < 2; ++h) {
+              float4 v = pend[h * 128 + t];
               v.x = __fmul_rn(v.x, alpha); v.y = __fmul_rn(v.y, alpha);
               v.z = __fmul_rn(v.z, alpha); v.w = __fmul_rn(v.w, alpha);
-              pend[(2 * h + q4) * 128 + t] = v;
+              pend[h * 128 + t] = v;
             }
           }
           reinterpret_cast<float*>(pend + (slot >> 2) * 128 + t)[slot & 3] =
               __fmul_rn(__fsub_rn(dcur, dbuf[(b ^ 1) * 128 + t]), alpha);
+          if (slot == 7) {
+            write_mass_operand(smem + L::kOffMassA, pend, t, 8);
+            mbar_arrive(&bar->a_full);
+          }
         }
         // the denominator column just before PV(j), for the group of tile j+1
         dbuf[b * 128 + t] = j >= 1 ? __fmul_rn(dcur, alpha) : 0.f;
@@ -532,15 +531,10 @@ __global__ void __launch_bounds__(kAltThreads, 1)
           const float dlast = __uint_as_float(tmem_ld1(tmem + lane_base + kAColO + D));
           tmem_wait_ld();
           float4* pend = reinterpret_cast<float4*>(smem + L::kOffPend);
-          const int slot = (T - 1) & 15;
+          const int slot = (T - 1) & 7;
           reinterpret_cast<float*>(pend + (slot >> 2) * 128 + t)[slot & 3] =
               __fsub_rn(dlast, reinterpret_cast<const float*>(smem + L::kOffD)[((T - 1) & 1) * 128 + t]);
-          const int kl = (T - 1) >> 3;
-          const int kf = (((T - 1) & 7) == 0 && kl >= 1) ? kl - 1 : kl;
-          for (int kb = kf; kb <= kl; ++kb)
-            write_mass_operand(smem + L::kOffMassA + (kb & 1) * L::kMassA, pend, kb & 1, t,
-                               kb < kl ? 8 : ((T - 1) & 7) + 1, 1.f);
-          fence_proxy_async_smem();
+          write_mass_operand(smem + L::kOffMassA, pend, t, slot + 1);
           tc_fence_before();
           mbar_arrive(&bar->p_full[T & 1]);
         }
