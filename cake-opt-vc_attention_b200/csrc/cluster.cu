@@ -51,100 +51,164 @@ __device__ __forceinline__ float sum_four(float x) {
   return __fadd_rn(x, __shfl_xor_sync(0xffffffffu, x, 2, 4));
 }
 
+// 16-byte asynchronous copy global -> shared; src_bytes 0 writes zeros.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// Row stride of the staged tile: the row plus 16 bytes, so that 8 threads
+// reading 16 bytes of 8 consecutive rows hit 8 different bank quads.
+template <typename T, int D>
+struct GrpTile {
+  static constexpr int kRowBytes = D * int(sizeof(T)) + 16;
+  static constexpr int kChunks = D * int(sizeof(T)) / 16;   // 16-byte chunks per row
+  static constexpr int kEl = 16 / int(sizeof(T));           // elements per chunk
+  static constexpr int kBytes = kRows * kRowBytes;
+  static constexpr int kSmem = kMaxC * D * 4 + kMaxC * 4 + kBytes + kRows * 4;
+};
+
+// 16 bytes of a staged row as floats (exact conversions).
+template <typename T>
+__device__ __forceinline__ void chunk_f32(const uint8_t* p, float (&x)[16 / sizeof(T)]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[i] = __uint_as_float(w[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      T lo, hi;
+      const uint16_t a = static_cast<uint16_t>(w[i] & 0xffffu), b = static_cast<uint16_t>(w[i] >> 16);
+      memcpy(&lo, &a, 2);
+      memcpy(&hi, &b, 2);
+      x[2 * i] = to_f32(lo);
+      x[2 * i + 1] = to_f32(hi);
+    }
+  }
+}
+
 // Assign each token of a 128-token tile to its nearest centre.  With STATS,
 // also write this tile's per-centre channel sums and counts, accumulated by
 // thread d over the tile's rows in token order.
+//
+// The tile is staged in its input type by cp.async (every copy in flight at
+// once).  Thread r owns token r: for every centre it keeps the four partial
+// dot products of channel residues 0..3 (channel 4j+l feeds partial l, in j
+// order) and the four partial squared norms, and combines each as
+// (p0 + p1) + (p2 + p3) -- the arithmetic of four lanes per row reduced by
+// xor-shuffles, computed by one thread.
 template <typename T, int D, bool STATS>
 __global__ void __launch_bounds__(128) grp_assign(const T* __restrict__ v, int64_t H, int64_t S, int64_t sb, int64_t sh,
                                                   int64_t ss, int count, const float* __restrict__ centers,
                                                   int32_t* __restrict__ labels, float* __restrict__ psum,
                                                   int32_t* __restrict__ pcnt, int64_t tiles) {
-  extern __shared__ __align__(16) float grp_smem[];
-  float(*cen)[D] = reinterpret_cast<float(*)[D]>(grp_smem);
-  float* cnorm = grp_smem + kMaxC * D;
-  float(*xs)[D + 1] = reinterpret_cast<float(*)[D + 1]>(grp_smem + kMaxC * D + kMaxC);
-  int* lab = reinterpret_cast<int*>(grp_smem + kMaxC * D + kMaxC + kRows * (D + 1));
+  using L = GrpTile<T, D>;
+  extern __shared__ __align__(16) uint8_t grp_raw[];
+  float(*cen)[D] = reinterpret_cast<float(*)[D]>(grp_raw);
+  float* cnorm = reinterpret_cast<float*>(grp_raw + kMaxC * D * 4);
+  uint8_t* xs = grp_raw + kMaxC * D * 4 + kMaxC * 4;
+  int* lab = reinterpret_cast<int*>(xs + L::kBytes);
   const int64_t bh = blockIdx.y, tile = blockIdx.x;
   const int64_t b = bh / H, h = bh - b * H;
-  const int lane = threadIdx.x & 3, group = threadIdx.x >> 2;
-  for (int i = threadIdx.x; i < kMaxC * D; i += 128)
-    cen[i / D][i % D] = i < count * D ? centers[bh * count * D + i] : 0.f;
-  // stage the tile as FP32 (zeros past S)
-  constexpr int EPT = 16 / sizeof(T);
-  constexpr int CPR = D / EPT;
-  for (int i = threadIdx.x; i < kRows * CPR; i += 128) {
-    const int r = i / CPR, c = i % CPR;
+  const T* vbh = v + b * sb + h * sh;
+  for (int i = threadIdx.x; i < kRows * L::kChunks; i += 128) {
+    const int r = i / L::kChunks, c = i - r * L::kChunks;
     const int64_t row = tile * kRows + r;
-    float x[EPT];
-    if (row < S) {
-      load_vec<T, EPT>(v + b * sb + h * sh + row * ss + c * EPT, x);
-    } else {
-#pragma unroll
-      for (int e = 0; e < EPT; ++e) x[e] = 0.f;
+    const bool in = row < S;
+    cp_async16(xs + r * L::kRowBytes + c * 16, vbh + (in ? row : 0) * ss + c * L::kEl, in ? 16u : 0u);
+  }
+  for (int i = threadIdx.x; i < kMaxC * D / 4; i += 128) {
+    const bool in = i < count * D / 4;
+    cp_async16(&cen[0][0] + i * 4, centers + bh * count * D + (in ? i * 4 : 0), in ? 16u : 0u);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    // |c|^2 with four lanes per centre (lane l: channels 4j+l in j order)
+    const int lane = threadIdx.x & 3, group = threadIdx.x >> 2;
+    float cn = 0.f;
+#pragma unroll 8
+    for (int j = 0; j < D / 4; ++j) {
+      const float x = cen[group][j * 4 + lane];
+      cn = __fadd_rn(cn, __fmul_rn(x, x));
     }
-#pragma unroll
-    for (int e = 0; e < EPT; ++e) xs[r][c * EPT + e] = x[e];
+    cn = sum_four(cn);
+    if (lane == 0) cnorm[group] = cn;
   }
   __syncthreads();
   {
-    float cn = 0.f;
-    if (group < kMaxC) {
-#pragma unroll 8
-      for (int j = 0; j < D / 4; ++j) {
-        const float x = cen[group][j * 4 + lane];
-        cn = __fadd_rn(cn, __fmul_rn(x, x));
+    const int r = threadIdx.x;
+    const int64_t row = tile * kRows + r;
+    const uint8_t* xrow = xs + r * L::kRowBytes;
+    float nrm[4] = {0.f, 0.f, 0.f, 0.f};
+    float dot[kMaxC][4];
+#pragma unroll
+    for (int c = 0; c < kMaxC; ++c)
+#pragma unroll
+      for (int l = 0; l < 4; ++l) dot[c][l] = 0.f;
+#pragma unroll 2
+    for (int k = 0; k < L::kChunks; ++k) {
+      float x[L::kEl];
+      chunk_f32<T>(xrow + k * 16, x);
+#pragma unroll
+      for (int q = 0; q < L::kEl / 4; ++q) {
+        const int j = k * (L::kEl / 4) + q;   // channels 4j .. 4j+3
+#pragma unroll
+        for (int l = 0; l < 4; ++l) nrm[l] = __fadd_rn(nrm[l], __fmul_rn(x[4 * q + l], x[4 * q + l]));
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c) {
+          const float4 cv = *reinterpret_cast<const float4*>(&cen[c][4 * j]);
+          dot[c][0] = __fmaf_rn(x[4 * q + 0], cv.x, dot[c][0]);
+          dot[c][1] = __fmaf_rn(x[4 * q + 1], cv.y, dot[c][1]);
+          dot[c][2] = __fmaf_rn(x[4 * q + 2], cv.z, dot[c][2]);
+          dot[c][3] = __fmaf_rn(x[4 * q + 3], cv.w, dot[c][3]);
+        }
       }
     }
-    cn = sum_four(cn);
-    if (group < kMaxC && lane == 0) cnorm[group] = cn;
-  }
-  __syncthreads();
-  for (int off = 0; off < kRows; off += 32) {
-    const int r = off + group;
-    const int64_t row = tile * kRows + r;
-    // all centres' dot products advance together (8 independent FMA chains);
-    // each one still sums its lane's elements in the same order
-    float norm = 0.f;
-    float dot[kMaxC];
-#pragma unroll
-    for (int c = 0; c < kMaxC; ++c) dot[c] = 0.f;
-#pragma unroll 4
-    for (int j = 0; j < D / 4; ++j) {
-      const float x = xs[r][j * 4 + lane];
-      norm = __fadd_rn(norm, __fmul_rn(x, x));
-#pragma unroll
-      for (int c = 0; c < kMaxC; ++c) dot[c] = __fmaf_rn(x, cen[c][j * 4 + lane], dot[c]);
-    }
-    norm = sum_four(norm);
+    const float norm = __fadd_rn(__fadd_rn(nrm[0], nrm[1]), __fadd_rn(nrm[2], nrm[3]));
     float best_d = __int_as_float(0x7f800000);
     int best = 0;
 #pragma unroll
     for (int c = 0; c < kMaxC; ++c) {
-      const float dc = sum_four(dot[c]);
+      const float dc = __fadd_rn(__fadd_rn(dot[c][0], dot[c][1]), __fadd_rn(dot[c][2], dot[c][3]));
       const float dist = __fsub_rn(__fadd_rn(norm, cnorm[c]), __fmul_rn(2.f, dc));
       if (c < count && dist < best_d) {
         best_d = dist;
         best = c;
       }
     }
-    best = __shfl_sync(0xffffffffu, best, 0, 4);
-    if (lane == 0) {
-      lab[r] = row < S ? best : -1;
-      if (row < S) labels[bh * S + row] = best;
-    }
+    lab[r] = row < S ? best : -1;
+    if (row < S) labels[bh * S + row] = best;
   }
   if constexpr (STATS) {
     __syncthreads();
+    // thread d sums channel d of each centre's rows in token order; the
+    // label is the same for the whole warp, so the switch does not diverge
     for (int d = threadIdx.x; d < D; d += 128) {
       float acc[kMaxC];
 #pragma unroll
       for (int c = 0; c < kMaxC; ++c) acc[c] = 0.f;
+      const uint8_t* col = xs + (d / L::kEl) * 16 + (d % L::kEl) * int(sizeof(T));
       for (int r = 0; r < kRows; ++r) {
-        const int c = lab[r];
-        const float x = xs[r][d];
-#pragma unroll
-        for (int cc = 0; cc < kMaxC; ++cc)
-          if (cc == c) acc[cc] = __fadd_rn(acc[cc], x);
+        T e;
+        memcpy(&e, col + r * L::kRowBytes, sizeof(T));
+        const float x = to_f32(e);
+        switch (lab[r]) {
+          case 0: acc[0] = __fadd_rn(acc[0], x); break;
+          case 1: acc[1] = __fadd_rn(acc[1], x); break;
+          case 2: acc[2] = __fadd_rn(acc[2], x); break;
+          case 3: acc[3] = __fadd_rn(acc[3], x); break;
+          case 4: acc[4] = __fadd_rn(acc[4], x); break;
+          case 5: acc[5] = __fadd_rn(acc[5], x); break;
+          case 6: acc[6] = __fadd_rn(acc[6], x); break;
+          case 7: acc[7] = __fadd_rn(acc[7], x); break;
+          default: break;
+        }
       }
 #pragma unroll
       for (int c = 0; c < kMaxC; ++c)
@@ -241,7 +305,7 @@ int launch_group(const GroupArgs& a, cudaStream_t st) {
   w += ((BH * tiles * kMaxC * 4 + 255) / 256) * 256;
   int32_t* hist = reinterpret_cast<int32_t*>(w);
   const T* v = static_cast<const T*>(a.v);
-  const int smem = (kMaxC * D + kMaxC + kRows * (D + 1) + kRows) * 4;
+  const int smem = GrpTile<T, D>::kSmem;
   cudaFuncSetAttribute(grp_assign<T, D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   cudaFuncSetAttribute(grp_assign<T, D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (a.centers_in)
