@@ -11,17 +11,19 @@
 //               an mbarrier per tile parity and per warp (a warp needs only
 //               its own 32 rows, so no warp waits for another warp's skew)
 //   warp 8      K producer (TMA, 4-deep ring);  warp 10  V producer (3-deep)
-//   warp 9      TMEM allocator + QK^T issuer: QK(j) is issued as soon as K(j)
-//               has landed and the scores of tile j-2 have been read
+//   warp 9      TMEM allocator + QK^T issuer: preset + QK(j) are issued as
+//               soon as K(j) has landed and the scores of tile j-2 have been read
 //   warp 11     P.V issuer: PV(j) as soon as P(j) and V(j) are ready
 //
 // Tensor memory (496 of 512 columns):
-//   S0 [0,128) S1 [128,256)   s32 scores of tiles j%2.  Each buffer is preset
-//                             to 0x4B400000 (the bits of 1.5*2^23) and QK^T
-//                             accumulates onto it, so the scores arrive as
-//                             the bit patterns of 1.5*2^23 + s: floats
-//                             without an int->float conversion.  The softmax
-//                             group re-presets a buffer right after reading it.
+//   S0 [0,128) S1 [128,256)   s32 scores of tiles j%2.  Before QK(j) the
+//                             QK^T issuer presets S[j%2] to 0x4B400000 (the
+//                             bits of 1.5*2^23) with one kind::f16 MMA,
+//                             A.B^T = 2048 x 6144 from constant shared-memory
+//                             operands, and QK^T accumulates onto it, so the
+//                             scores arrive as the bit patterns of
+//                             1.5*2^23 + s: floats without an int->float
+//                             conversion and without register fills.
 //   O  [256,256+D+16)         FP32 accumulator for the whole K loop; column D
 //                             accumulates P.1 (the ExpCast denominator) via a
 //                             row of E4M3 1.0 appended to every V tile
@@ -100,7 +102,11 @@ struct AltSmem {
   static constexpr int kOffMassA = kOffPend + 2 * 128 * 16;
   static constexpr int kMean = D * 32;                       // D x 16 FP16 (mean, mean) x 8 tiles
   static constexpr int kOffMean = kOffMassA + kMassA;        // two batch buffers
-  static constexpr int kOffBar = kOffMean + 2 * kMean;
+  // score preset operands: 128 x 16 FP16 each, element 0 of every row set
+  // (2048 in A, 6144 in B), so A.B^T = 12582912 = 1.5*2^23 everywhere
+  static constexpr int kOffPresetA = kOffMean + 2 * kMean;
+  static constexpr int kOffPresetB = kOffPresetA + 128 * 32;
+  static constexpr int kOffBar = kOffPresetB + 128 * 32;
   static constexpr int kOffSlot = kOffBar + int(sizeof(AltBarriers));
   static constexpr int kBytes = kOffSlot + 16;
   static constexpr int kAlloc = kBytes + 1024;
@@ -173,6 +179,12 @@ __global__ void __launch_bounds__(kAltThreads, 1)
     const int s = i / (16 * 8), r = (i / 8) % 16, c = i % 8;
     const uint32_t fill = r == 0 ? 0x38383838u : 0u;   // E4M3 1.0 in row D, zeros below
     *reinterpret_cast<uint4*>(smem + L::kOffV + s * L::kV + (D + r) * 128 + c * 16) = make_uint4(fill, fill, fill, fill);
+  }
+  for (int r = threadIdx.x; r < 128; r += kAltThreads) {
+    *reinterpret_cast<uint4*>(smem + L::kOffPresetA + plain32_offset(r)) = make_uint4(0x6800u, 0, 0, 0);   // FP16 2048
+    *reinterpret_cast<uint4*>(smem + L::kOffPresetA + plain32_offset(r) + 128) = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(smem + L::kOffPresetB + plain32_offset(r)) = make_uint4(0x6E00u, 0, 0, 0);   // FP16 6144
+    *reinterpret_cast<uint4*>(smem + L::kOffPresetB + plain32_offset(r) + 128) = make_uint4(0, 0, 0, 0);
   }
   if constexpr (BV) {
     // zero the pending masses and the FP16 operands once
@@ -254,17 +266,21 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       // QK(j) goes as soon as K(j) has landed and the scores of tile j-2 have
       // been read out of S[j%2].
       constexpr uint32_t idesc_qk = idesc_make(2, 1, 1, 128, 128);     // s32 <- s8 x s8
+      constexpr uint32_t idesc_preset = idesc_make(1, 0, 0, 128, 128); // f32 <- f16 x f16
+      const uint64_t adesc_preset = smem_desc_plain(smem_u32(smem + L::kOffPresetA), 128, 256);
+      const uint64_t bdesc_preset = smem_desc_plain(smem_u32(smem + L::kOffPresetB), 128, 256);
       const uint64_t kdesc0 = kmajor_desc<D>(smem_u32(smem + L::kOffK));
       constexpr uint64_t kStepK = (L::kK >> 4);                         // descriptor start-address units
       if (mbar_wait(&bar->q_ready, 0, kErrTimeoutMma)) {
         for (int j = 0; j < T; ++j) {
           const int s = j % kKS, b = j & 1;
           if (!mbar_wait(&bar->k_full[s], (j / kKS) & 1, kErrTimeoutMma)) break;
-          // completion (j>>1) of s_free[b]: the preset after tile j-2 was read (or the initial one)
+          // completion (j>>1) of s_free[b]: the scores of tile j-2 were read (or the initial release)
           if (!mbar_wait(&bar->s_free[b], (j >> 1) & 1, kErrTimeoutMma)) break;
           tc_fence_after();
           const uint64_t kd = kdesc0 + s * kStepK;
           const uint32_t scol = tmem + (b ? kAColS1 : kAColS0);
+          mma_f16_ss(scol, adesc_preset, bdesc_preset, idesc_preset, 0u);   // S = the bits of 1.5*2^23
 #pragma unroll
           for (int kk = 0; kk < D / 32; ++kk)
             mma_i8_ts(scol, tmem + kAColQ + kk * 8, kd + 2 * kk, idesc_qk, 1u);   // onto the preset
@@ -348,15 +364,7 @@ __global__ void __launch_bounds__(kAltThreads, 1)
     const uint64_t bias2 = pk2f(kBias, kBias);
     const uint64_t tiny2 = pk2(kDenormOne, kDenormOne);
     const uint64_t expa2 = pk2f(kExpA, kExpA), expb2 = pk2f(kExpB, kExpB);
-    {
-      // preset this group's score buffer S[w] for its first tile
-      const uint32_t scol = tmem + lane_base + (w ? kAColS1 : kAColS0);
-#pragma unroll
-      for (int c = 0; c < 128; c += 32) tmem_fill32(scol + c, kBiasBits);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&bar->s_free[w]);
-    }
+    mbar_arrive(&bar->s_free[w]);   // S[w] is free for this group's first tile
     bool ok = true;
     float4 ksv_next = w < T ? __ldg(reinterpret_cast<const float4*>(p.ks + bh * p.nks + w * 4)) : make_float4(1, 1, 1, 1);
     for (int j = w; j < T; j += 2) {
@@ -373,9 +381,8 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       tmem_ld32(scol + 64, *reinterpret_cast<uint32_t(*)[32]>(raw + 64));
       tmem_ld32(scol + 96, *reinterpret_cast<uint32_t(*)[32]>(raw + 96));
       tmem_wait_ld();
-      // preset S[b] again for QK(j+2); released once the stores have landed (below)
-#pragma unroll
-      for (int c = 0; c < 128; c += 32) tmem_fill32(scol + c, kBiasBits);
+      tc_fence_before();
+      mbar_arrive(&bar->s_free[b]);   // QK(j+2) may now overwrite S[b]
       if (j == T - 1) {
         const int valid = static_cast<int>(p.Sk - int64_t(j) * 128);
 #pragma unroll
@@ -396,9 +403,6 @@ __global__ void __launch_bounds__(kAltThreads, 1)
           mx = max3f(mx, __uint_as_float(raw[8 * k + 2 * g]), __uint_as_float(raw[8 * k + 2 * g + 1]));
         if (mx > 0.f) lmax = fmaxf(lmax, __fmul_rn(__fsub_rn(mx, kBias), f1[g]));
       }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&bar->s_free[b]);   // QK(j+2) may now accumulate onto the preset
       // running maximum handed over from the other group's previous tile
       float mprev = -5000000.0f;
       if (j >= 1) {

@@ -47,8 +47,7 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-constexpr uint32_t kBiasBits = 0x4B400000u;   // 1.5 * 2^23
-constexpr float kBias = 12582912.0f;
+constexpr float kBias = 12582912.0f;   // 1.5 * 2^23: the score preset, bits 0x4B400000
 
 template <uint32_t N>
 __device__ __forceinline__ void setmaxnreg_inc() {
