@@ -335,6 +335,24 @@ def main():
                 o = parallel.sharded_attention(dq, dk, dv, local_shard, v_smooth=smooth)
                 hout.copy_(o, non_blocking=True)
 
+        # the host link alone: one pinned-host -> device copy of the inputs and one
+        # device -> pinned-host copy of the output, the floor for the end-to-end time
+        link = {}
+        dq_l = torch.empty_like(q)
+        for name, fn, nbytes in (("h2d_gbs", lambda: [d.copy_(h, non_blocking=True) for d, h in
+                                                      ((dq_l, hq), (dq_l, hk), (dq_l, hv))],
+                                  3 * q.numel() * q.element_size()),
+                                 ("d2h_gbs", lambda: hout.copy_(dq_l.view(hout.shape), non_blocking=True),
+                                  q.numel() * q.element_size())):
+            fn()
+            torch.cuda.synchronize()
+            l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            l0.record()
+            fn()
+            l1.record()
+            torch.cuda.synchronize()
+            link[name] = nbytes / (l0.elapsed_time(l1) * 1e-3) / 1e9
+        del dq_l
         for _ in range(2):
             e2e_step()
         torch.cuda.synchronize()
@@ -356,7 +374,8 @@ def main():
                "h2d_bytes_per_step": 3 * nbh * S * D * q.element_size(),
                "d2h_bytes_per_step": nbh * S * D * q.element_size(),
                "path": ("vc_b200.pipeline.sageattn_vc_host on pinned-host inputs (head chunks, copies overlapped)"
-                        if world == 1 else "per-rank sharded_attention on pinned-host inputs")}
+                        if world == 1 else "per-rank sharded_attention on pinned-host inputs"),
+               "link_gbs_measured": link}
 
     gather_ms = None
     if args.gather and dist:
