@@ -51,15 +51,6 @@ __device__ __forceinline__ float sum_four(float x) {
   return __fadd_rn(x, __shfl_xor_sync(0xffffffffu, x, 2, 4));
 }
 
-// 16-byte asynchronous copy global -> shared; src_bytes 0 writes zeros.
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-}
-
 // Row stride of the staged tile: the row plus 16 bytes, so that 8 threads
 // reading 16 bytes of 8 consecutive rows hit 8 different bank quads.
 template <typename T, int D>

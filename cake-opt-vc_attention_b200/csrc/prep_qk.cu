@@ -192,7 +192,6 @@ __global__ void __launch_bounds__(kTileThreads, 1) qk_tiles(QKTileParams p) {
     int n = 0;
     for (int64_t t = blockIdx.x; t < p.total; t += gridDim.x, ++n) {
       const int s = n % L::kStages;
-      if (n >= L::kStages && !mbar_wait(&empty[s], ((n / L::kStages) & 1) ^ 1, kErrTimeoutProducer)) break;
       const bool isq = t < p.nq;
       const int64_t tt = isq ? t : t - p.nq;
       const int64_t tiles = isq ? p.qtiles : p.ktiles;
@@ -202,23 +201,34 @@ __global__ void __launch_bounds__(kTileThreads, 1) qk_tiles(QKTileParams p) {
       const int64_t b = bh / p.H, h = bh - b * p.H;
       const T* base = static_cast<const T*>(isq ? p.q : p.k) + b * (isq ? p.qsb : p.ksb) + h * (isq ? p.qsh : p.ksh);
       const int64_t ss = isq ? p.qss : p.kss;
+      const bool contiguous = ss == D && (isq || !p.perm);
+      // source rows of this lane (rows lane + 32i), the permutation entries
+      // loaded before the slot wait so that their latency overlaps it
+      int64_t src[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = lane + 32 * i;
+        src[i] = r0 + r;
+        if (!contiguous && !isq && p.perm && r < rows) src[i] = __ldg(p.perm + bh * S + r0 + r);
+      }
+      if (n >= L::kStages && !mbar_wait(&empty[s], ((n / L::kStages) & 1) ^ 1, kErrTimeoutProducer)) break;
       if (lane == 0) mbar_expect_tx(&full[s], static_cast<uint32_t>(rows * L::kRow));
       __syncwarp();
       uint8_t* dst = sm + s * L::kStage;
-      if (ss == D && (isq || !p.perm)) {   // contiguous rows: one copy for the tile
+      if (contiguous) {   // contiguous rows: one copy for the tile
         if (lane == 0) bulk_load(dst, base + r0 * ss, static_cast<uint32_t>(rows * L::kRow), &full[s]);
         continue;
       }
-      for (int r = lane; r < rows; r += 32) {
-        int64_t src = r0 + r;
-        if (!isq && p.perm) {
-          src = p.perm[bh * S + src];
-          if (src < 0 || src >= S) {
-            raise_error(kErrBadIndex);   // out-of-range permutation entry: read row 0 instead
-            src = 0;
-          }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = lane + 32 * i;
+        if (r >= rows) break;
+        int64_t sr = src[i];
+        if (sr < 0 || sr >= S) {
+          raise_error(kErrBadIndex);   // out-of-range permutation entry: read row 0 instead
+          sr = 0;
         }
-        bulk_load(dst + r * L::kRow, base + src * ss, L::kRow, &full[s]);
+        bulk_load(dst + r * L::kRow, base + sr * ss, L::kRow, &full[s]);
       }
     }
     return;

@@ -24,28 +24,39 @@ struct TileGeom {
   static constexpr int kSmem = kInBytes + kOutBytes + 4 * D * 4;
 };
 
-// Stage rows [tile*128, tile*128+128) of head bh into smem (zeros past S).
+// Stage rows [tile*128, tile*128+128) of head bh into smem (zeros past S and
+// for out-of-range permutation entries, which also raise kErrBadIndex).  Each
+// thread first loads the source indices of all its chunks, then issues every
+// chunk as a cp.async, so no load waits on another; the caller synchronises.
 template <typename T, int D>
 __device__ __forceinline__ void stage_tile(uint8_t* sin, const T* __restrict__ v, int64_t bh, int64_t H, int64_t S,
                                            int64_t sb, int64_t sh, int64_t ss, const int64_t* __restrict__ perm,
                                            int64_t tile) {
   using G = TileGeom<T, D>;
   constexpr int CPR = G::kRowBytes / 16;  // 16-byte chunks per row
+  constexpr int EL = 16 / int(sizeof(T));
+  constexpr int IT = (128 * CPR + kTileThreads - 1) / kTileThreads;
   const int64_t b = bh / H, h = bh - b * H;
   const T* base = v + b * sb + h * sh;
-  for (int i = threadIdx.x; i < 128 * CPR; i += blockDim.x) {
-    const int r = i / CPR, c = i % CPR;
-    const int64_t row = tile * 128 + r;
-    uint4 val = make_uint4(0, 0, 0, 0);
-    if (row < S) {
-      const int64_t src = perm ? perm[bh * S + row] : row;
-      if (src >= 0 && src < S)
-        val = __ldg(reinterpret_cast<const uint4*>(base + src * ss) + c);
-      else
-        raise_error(kErrBadIndex);
-    }
-    *reinterpret_cast<uint4*>(sin + r * G::kPitch + c * 16) = val;
+  int64_t src[IT];
+#pragma unroll
+  for (int k = 0; k < IT; ++k) {
+    const int i = threadIdx.x + k * kTileThreads;
+    const int64_t row = tile * 128 + i / CPR;
+    src[k] = -1;
+    if (i < 128 * CPR && row < S) src[k] = perm ? __ldg(perm + bh * S + row) : row;
   }
+#pragma unroll
+  for (int k = 0; k < IT; ++k) {
+    const int i = threadIdx.x + k * kTileThreads;
+    if (i >= 128 * CPR) break;
+    const int r = i / CPR, c = i - r * CPR;
+    const bool in = tile * 128 + r < S;
+    const bool ok = src[k] >= 0 && src[k] < S;
+    if (in && !ok) raise_error(kErrBadIndex);
+    cp_async16(sin + r * G::kPitch + c * 16, base + (ok ? src[k] : 0) * ss + c * EL, ok ? 16u : 0u);
+  }
+  cp_async_wait_all();
 }
 
 template <typename T>
