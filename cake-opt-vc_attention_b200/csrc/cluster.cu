@@ -244,17 +244,25 @@ __global__ void grp_hist(const int32_t* __restrict__ labels, int64_t S, int coun
   if (threadIdx.x < count) hist[(bh * nchunk + chunk) * count + threadIdx.x] = h[threadIdx.x];
 }
 
-// Step 2: exclusive offsets, cluster-major then chunk order.
+// Step 2: exclusive offsets, cluster-major then chunk order.  One warp per
+// head: 32 chunks at a time, an inclusive shuffle scan plus the running total.
 __global__ void grp_scan(int32_t* __restrict__ hist, int count, int64_t nchunk) {
   const int64_t bh = blockIdx.x;
-  if (threadIdx.x != 0) return;
-  int64_t run = 0;
+  const int lane = threadIdx.x;
+  int32_t run = 0;
   for (int c = 0; c < count; ++c)
-    for (int64_t k = 0; k < nchunk; ++k) {
+    for (int64_t k0 = 0; k0 < nchunk; k0 += 32) {
+      const int64_t k = k0 + lane;
       int32_t* p = hist + (bh * nchunk + k) * count + c;
-      const int32_t n = *p;
-      *p = static_cast<int32_t>(run);
-      run += n;
+      const int32_t n = k < nchunk ? *p : 0;
+      int32_t incl = n;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      if (k < nchunk) *p = run + incl - n;
+      run += __shfl_sync(0xffffffffu, incl, 31);
     }
 }
 

@@ -12,8 +12,20 @@ from __future__ import annotations
 import torch
 
 
+_STREAMS: dict[int, tuple] = {}
+
+
 def _chunks(n: int, size: int):
     return [(i, min(n, i + size)) for i in range(0, n, size)]
+
+
+def _streams(device: torch.device):
+    """The copy-in, compute and copy-out streams of ``device``, created once:
+    PyTorch's caching allocator keeps a block pool per stream, so fresh
+    streams on every call would send every chunk's allocations to cudaMalloc."""
+    if device.index not in _STREAMS:
+        _STREAMS[device.index] = tuple(torch.cuda.Stream(device) for _ in range(3))
+    return _STREAMS[device.index]
 
 
 def sageattn_vc_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor | None = None, *,
@@ -34,12 +46,14 @@ def sageattn_vc_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: tor
     if chunk_heads < 1:
         raise ValueError("chunk_heads must be positive")
     device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    if device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
     B, H = q.shape[:2]
     if out is None:
         out = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
     # flatten (B, H) so chunks are contiguous slices of heads
     qf, kf, vf, of = (x.reshape(B * H, *x.shape[2:]) for x in (q, k, v, out))
-    h2d, comp, d2h = (torch.cuda.Stream(device) for _ in range(3))
+    h2d, comp, d2h = _streams(device)
     pending = []
     with torch.cuda.device(device):
         for a, b in _chunks(B * H, chunk_heads):
