@@ -331,9 +331,10 @@ def main():
                 from vc_b200.pipeline import sageattn_vc_host
                 sageattn_vc_host(hq, hk, hv, hout, device=dev, v_smooth=smooth)
             else:
-                dq, dk, dv = (x.to(dev, non_blocking=True) for x in (hq, hk, hv))
-                o = parallel.sharded_attention(dq, dk, dv, local_shard, v_smooth=smooth)
-                hout.copy_(o, non_blocking=True)
+                # this rank's unit range on its host-resident heads, copies overlapped the same way
+                from vc_b200.pipeline import sharded_attention_host
+                sharded_attention_host(hq, hk, hv, hout, local_shard.local_units, device=dev,
+                                       mean_numel=mean_numel, v_smooth=smooth)
 
         # the host link alone: one pinned-host -> device copy of the inputs and one
         # device -> pinned-host copy of the output, the floor for the end-to-end time
@@ -374,7 +375,8 @@ def main():
                "h2d_bytes_per_step": 3 * nbh * S * D * q.element_size(),
                "d2h_bytes_per_step": nbh * S * D * q.element_size(),
                "path": ("vc_b200.pipeline.sageattn_vc_host on pinned-host inputs (head chunks, copies overlapped)"
-                        if world == 1 else "per-rank sharded_attention on pinned-host inputs"),
+                        if world == 1 else
+                        "vc_b200.pipeline.sharded_attention_host per rank on pinned-host inputs (head chunks, copies overlapped)"),
                "link_gbs_measured": link}
 
     gather_ms = None

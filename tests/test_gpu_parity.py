@@ -501,3 +501,32 @@ def test_host_pipeline_equals_one_call(ops, smooth):
     got = sageattn_vc_host(hq, hk, hv, chunk_heads=3, v_smooth=smooth)
     want = sageattn_vc(q.cuda(), k.cuda(), v.cuda(), v_smooth=smooth)
     assert got.device.type == "cpu" and torch.equal(got, want.cpu())
+
+
+@pytest.mark.parametrize("smooth", [False, True])
+def test_sharded_host_pipeline_equals_device_shards(ops, smooth):
+    """sharded_attention_host computes exactly a rank's unit range: for every
+    rank of a 3-way split (ranges that cut through heads), its rows equal
+    the single sageattn_vc call bit for bit, and it writes no other row."""
+    from sageattention_local import sageattn_vc
+    from vc_b200 import parallel as P
+    from vc_b200.pipeline import sharded_attention_host
+    shape = (1, 5, 700, 128)
+    B, H, S, D = shape
+    q, k, _ = qk_inputs(44, shape, torch.bfloat16, 3 ** 0.5)
+    v = mixture_values(44, shape, torch.bfloat16)
+    hq, hk, hv = (x.pin_memory() for x in (q, k, v))
+    want = sageattn_vc(q.cuda(), k.cuda(), v.cuda(), v_smooth=smooth).cpu()
+    mean_numel = (B * H * D, B * H * S * D)
+    covered = torch.zeros(B * H * S, dtype=torch.bool)
+    for rank in range(3):
+        s = P.shard(B, H, S, 3, rank)
+        out = torch.full(shape, float("nan"), dtype=torch.bfloat16).pin_memory()
+        sharded_attention_host(hq, hk, hv, out, (s.unit_begin, s.unit_end), chunk_heads=2,
+                               mean_numel=mean_numel, v_smooth=smooth)
+        r0, r1 = P.shard_rows(s, S)
+        got, ref = out.view(-1, D), want.view(-1, D)
+        assert torch.equal(got[r0:r1], ref[r0:r1])
+        assert torch.isnan(got[:r0].float()).all() and torch.isnan(got[r1:].float()).all()
+        covered[r0:r1] = True
+    assert covered.all()

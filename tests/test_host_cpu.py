@@ -238,3 +238,18 @@ def test_gather_rows_gloo_world2(B, H, S):
     for p in procs:
         p.join(timeout=60)
     assert results == {0: True, 1: True}, results
+
+
+def test_sharded_host_pipeline_rejects_bad_arguments():
+    """Argument checks of sharded_attention_host happen before any device use."""
+    from vc_b200.pipeline import sharded_attention_host
+    x = torch.zeros(1, 2, 200, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        sharded_attention_host(x, x, x, x, (0, 5))          # 2 heads x 2 tiles = 4 units
+    with pytest.raises(ValueError):
+        sharded_attention_host(x, x, x, x, (3, 2))
+    with pytest.raises(ValueError):
+        sharded_attention_host(x, x, x[:, :1], x, (0, 1))
+    with pytest.raises(ValueError):
+        sharded_attention_host(x, x, x, x, (0, 1), chunk_heads=0)
+    assert sharded_attention_host(x, x, x, x, (2, 2)) is x   # empty range: nothing to do
