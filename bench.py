@@ -43,9 +43,10 @@ CONFIGS = {
            "BNSD [1,28,37741,128] bf16, ExpCast on, smoothing off"),
     "c3": (1, 28, 37741, 128, torch.bfloat16, 3 ** 0.5, True,
            "BNSD [1,28,37741,128] bf16, ExpCast + V grouping + 128-token block smoothing"),
-    "c4": (2, 24, 16384, 64, torch.bfloat16, 3 ** 0.5, False, "BNSD [2,24,16384,64] bf16 D64, ExpCast on"),
+    "c4": (2, 24, 16384, 64, torch.bfloat16, 3 ** 0.5, False,
+           "BNSD [2,24,16384,64] bf16 D64, ExpCast on, 1% of Q/K entries x20"),
     "c5": (2, 40, 75600, 128, torch.bfloat16, 3 ** 0.5, True,
-           "BNSD [2,40,75600,128] bf16, ExpCast + V block smoothing"),
+           "BNSD [2,40,75600,128] bf16, V ~ N(0,1), ExpCast + V grouping + block smoothing"),
 }
 METRIC = "TOPS (4*B*H*S^2*D per call) at BNSD [1,28,37741,128] D128, sageattn_vc ExpCast (prep + fused kernel)"
 
@@ -58,8 +59,18 @@ def peaks():
     return 6650.0, 1590.0, 1400.0, "fallback"
 
 
-def gen_head(bh: int, S: int, D: int, dtype, k_std: float, smooth: bool, device, seed: int = 0):
-    """Seeded synthetic Q,K,V for one flattened (b,h) head."""
+# per-config input distributions beyond the CONFIGS tuple (BASELINE's config definitions):
+# c3 draws V from a 16-centroid mixture; c4 scales 1% of the Q/K entries by 20
+GEN = {"c2": {}, "c3": {"v_mixture": True}, "c4": {"outliers": 0.01}, "c5": {}}
+
+
+def gen_head(bh: int, S: int, D: int, dtype, k_std: float, smooth: bool, device, seed: int = 0,
+             outliers: float = 0.0):
+    """Seeded synthetic Q,K,V for one flattened (b,h) head: Q ~ N(0,1), K ~ N(0,1)
+    plus a per-channel offset ~ N(0, k_std^2); V ~ N(0,1), or with ``smooth`` a
+    16-centroid mixture (centroids ~ N(0,2), within-cluster std 0.3).
+    ``outliers``: that fraction of the Q and K entries (Bernoulli mask from the
+    same generator) is multiplied by 20."""
     g = torch.Generator(device=device)
     g.manual_seed(seed * 1000003 + bh)
     q = torch.randn(S, D, generator=g, device=device)
@@ -70,6 +81,10 @@ def gen_head(bh: int, S: int, D: int, dtype, k_std: float, smooth: bool, device,
         v = cent[lab] + 0.3 * torch.randn(S, D, generator=g, device=device)
     else:
         v = torch.randn(S, D, generator=g, device=device)
+    if outliers > 0:
+        for x in (q, k):
+            mask = torch.rand(S, D, generator=g, device=device) < outliers
+            x[mask] *= 20.0
     return q.to(dtype), k.to(dtype), v.to(dtype)
 
 
@@ -159,13 +174,14 @@ class ClockSampler:
                 "samples": len(sm), "scope": scope}
 
 
-def cpu_baseline_sample(B, H, S, D, dtype, k_std, smooth, threads=None):
+def cpu_baseline_sample(B, H, S, D, dtype, k_std, smooth, threads=None, gen=None):
     """Time the CPU oracle on one head's preparation plus 128 query rows
     against all keys; extrapolate linearly to the full workload."""
     from oracle import vc_oracle as O
     if threads:
         torch.set_num_threads(threads)
-    q, k, v = gen_head(0, S, D, dtype, k_std, smooth, "cpu")
+    gen = gen or {}
+    q, k, v = gen_head(0, S, D, dtype, k_std, gen.get("v_mixture", False), "cpu", outliers=gen.get("outliers", 0.0))
     q, k, v = (x.reshape(1, 1, S, D) for x in (q, k, v))
     t0 = time.perf_counter()
     st = O.prepare(q, k, v, expcast=True, v_smooth=smooth, km=O.k_mean(k))
@@ -192,7 +208,7 @@ def run_reference(args, cfg):
     torch.set_num_threads(threads)
     vals = []
     for i in range(args.warmup + args.steps):
-        r = cpu_baseline_sample(B, H, S, D, dtype, k_std, smooth, threads)
+        r = cpu_baseline_sample(B, H, S, D, dtype, k_std, smooth, threads, GEN[args.config])
         if i >= args.warmup:
             vals.append(r)
     value = statistics.median(v["value"] for v in vals)
@@ -245,7 +261,8 @@ def main():
     # this rank's heads, generated on the device
     qh, kh, vh = [], [], []
     for bh in range(sh.bh_begin, sh.bh_end):
-        a, b_, c = gen_head(bh, S, D, dtype, k_std, smooth, dev)
+        a, b_, c = gen_head(bh, S, D, dtype, k_std, GEN[args.config].get("v_mixture", False), dev,
+                            outliers=GEN[args.config].get("outliers", 0.0))
         qh.append(a), kh.append(b_), vh.append(c)
     q = torch.stack(qh).reshape(1, nbh, S, D)
     k = torch.stack(kh).reshape(1, nbh, S, D)
@@ -390,7 +407,7 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_sample(B, H, S, D, dtype, k_std, smooth)
+        cpu = cpu_baseline_sample(B, H, S, D, dtype, k_std, smooth, gen=GEN[args.config])
 
     if rank == 0:
         # this library's kernels per step: K sums + mean finalize, Q/K tiles, then V channel amax +
