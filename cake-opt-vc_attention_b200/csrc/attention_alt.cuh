@@ -472,18 +472,20 @@ __global__ void __launch_bounds__(kAltThreads, 1)
         tc_fence_after();
         const uint32_t ocol = tmem + lane_base + kAColO;
         const uint64_t alpha2 = pk2f(alpha, alpha);
+        // all of O's columns in flight at once (the score registers are free by
+        // now): one tensor-memory load latency on the chain instead of D/32
+        uint32_t o[D];
 #pragma unroll
-        for (int cc = 0; cc < D / 32; ++cc) {
-          uint32_t o[32];
-          tmem_ld32(ocol + cc * 32, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) up2(f2_mul(pk2(o[2 * i], o[2 * i + 1]), alpha2), o[2 * i], o[2 * i + 1]);
-          tmem_st32(ocol + cc * 32, o);
-        }
+        for (int cc = 0; cc < D / 32; ++cc) tmem_ld32(ocol + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(o + cc * 32));
         // the denominator: column D (columns D+1.. of the block only ever hold zeros)
         if constexpr (!BV) draw = tmem_ld1(ocol + D);
         tmem_wait_ld_reg(draw);
+#pragma unroll
+        for (int cc = 0; cc < D / 32; ++cc) tmem_wait_ld_tie32(o + cc * 32);
+#pragma unroll
+        for (int i = 0; i < D / 2; ++i) up2(f2_mul(pk2(o[2 * i], o[2 * i + 1]), alpha2), o[2 * i], o[2 * i + 1]);
+#pragma unroll
+        for (int cc = 0; cc < D / 32; ++cc) tmem_st32(ocol + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(o + cc * 32));
         tmem_st1(ocol + D, __float_as_uint(__fmul_rn(__uint_as_float(draw), alpha)));
       }
       float4* pend = reinterpret_cast<float4*>(smem + L::kOffPend);
