@@ -56,6 +56,7 @@ struct Params {
   int64_t H, Sq, Sk;
   int64_t osb, osh, oss;
   int64_t nqs, nks, ktiles, qtiles;
+  int64_t kq_tiles;   // E4M3 block Q/K: K tiles per K scale
   int64_t unit_begin, unit_end;   // units (b*H+h)*qtiles + q_tile to compute
   float sm_scale;
   int exact_expcast;   // 1: unfused RN(RN(raw*f)-m) encoder instead of the folded affine one
@@ -493,9 +494,9 @@ struct Maps {
   CUtensorMap k, v;
 };
 
-template <int D, typename OutT, bool BV>
+template <int D, typename OutT, bool BV, bool QF8 = false>
 int launch_alt(const Maps& m, const Params& p, int64_t units, cudaStream_t st) {
-  auto k = vc_attention_alt_kernel<D, OutT, BV>;
+  auto k = vc_attention_alt_kernel<D, OutT, BV, QF8>;
   const int smem = AltSmem<D>::kAlloc;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return VC_ERR_LAUNCH;
   k<<<static_cast<unsigned>(units), kAltThreads, smem, st>>>(m.k, m.v, p);
@@ -504,6 +505,10 @@ int launch_alt(const Maps& m, const Params& p, int64_t units, cudaStream_t st) {
 
 template <int D, typename OutT>
 int dispatch_flags(const AttnArgs& a, const Maps& m, const Params& p, int64_t units, cudaStream_t st) {
+  if (a.qk_e4m3) {   // E4M3 block Q/K: the alternating-tile kernel only (ExpCast, channel V scales)
+    if (a.block_values) return launch_alt<D, OutT, true, true>(m, p, units, st);
+    return launch_alt<D, OutT, false, true>(m, p, units, st);
+  }
   if (a.expcast && !a.vs_per_block && !use_general_kernel()) {
     if (a.block_values) return launch_alt<D, OutT, true>(m, p, units, st);
     return launch_alt<D, OutT, false>(m, p, units, st);
@@ -553,8 +558,9 @@ int attention_fwd(const AttnArgs& a, cudaStream_t st) {
   p.osb = a.osb;
   p.osh = a.osh;
   p.oss = a.oss;
-  p.nqs = (a.Sq + 63) / 64 * 32;
-  p.nks = ktiles * 4;
+  p.nqs = a.qk_e4m3 ? qtiles : (a.Sq + 63) / 64 * 32;
+  p.nks = a.qk_e4m3 ? (a.Sk + a.kqb - 1) / a.kqb : ktiles * 4;
+  p.kq_tiles = a.qk_e4m3 ? a.kqb / 128 : 1;
   p.ktiles = ktiles;
   p.qtiles = qtiles;
   p.unit_begin = ub;

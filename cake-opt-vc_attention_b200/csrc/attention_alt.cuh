@@ -134,7 +134,7 @@ __device__ __forceinline__ void write_mass_operand(uint8_t* a, const float4* pen
   fence_proxy_async_smem();
 }
 
-template <int D, typename OutT, bool BV>
+template <int D, typename OutT, bool BV, bool QF8>
 __global__ void __launch_bounds__(kAltThreads, 1)
     vc_attention_alt_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                             Params p) {
@@ -265,7 +265,8 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       // ------------------------------------------------------- QK^T issuer
       // QK(j) goes as soon as K(j) has landed and the scores of tile j-2 have
       // been read out of S[j%2].
-      constexpr uint32_t idesc_qk = idesc_make(2, 1, 1, 128, 128);     // s32 <- s8 x s8
+      // s32 <- s8 x s8, or with E4M3 block Q/K f32 <- e4m3 x e4m3
+      constexpr uint32_t idesc_qk = QF8 ? idesc_make(1, 0, 0, 128, 128) : idesc_make(2, 1, 1, 128, 128);
       constexpr uint32_t idesc_preset = idesc_make(1, 0, 0, 128, 128); // f32 <- f16 x f16
       const uint64_t adesc_preset = smem_desc_plain(smem_u32(smem + L::kOffPresetA), 128, 256);
       const uint64_t bdesc_preset = smem_desc_plain(smem_u32(smem + L::kOffPresetB), 128, 256);
@@ -280,10 +281,17 @@ __global__ void __launch_bounds__(kAltThreads, 1)
           tc_fence_after();
           const uint64_t kd = kdesc0 + s * kStepK;
           const uint32_t scol = tmem + (b ? kAColS1 : kAColS0);
-          mma_f16_ss(scol, adesc_preset, bdesc_preset, idesc_preset, 0u);   // S = the bits of 1.5*2^23
+          if constexpr (QF8) {
+            // FP32 scores straight from the MMA: no preset
 #pragma unroll
-          for (int kk = 0; kk < D / 32; ++kk)
-            mma_i8_ts(scol, tmem + kAColQ + kk * 8, kd + 2 * kk, idesc_qk, 1u);   // onto the preset
+            for (int kk = 0; kk < D / 32; ++kk)
+              mma_f8_ts(scol, tmem + kAColQ + kk * 8, kd + 2 * kk, idesc_qk, kk > 0 ? 1u : 0u);
+          } else {
+            mma_f16_ss(scol, adesc_preset, bdesc_preset, idesc_preset, 0u);   // S = the bits of 1.5*2^23
+#pragma unroll
+            for (int kk = 0; kk < D / 32; ++kk)
+              mma_i8_ts(scol, tmem + kAColQ + kk * 8, kd + 2 * kk, idesc_qk, 1u);   // onto the preset
+          }
           mma_commit(&bar->k_empty[s]);
           mma_commit(&bar->s_full[b]);
         }
@@ -359,18 +367,28 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       tc_fence_before();
       mbar_arrive(&bar->q_ready);
     }
-    const float qscale = row_valid ? p.qs[bh * p.nqs + (row >> 4) * 8 + (row & 7)] : 0.f;
+    // INT8: the Sage per-thread Q scale of the row; E4M3 blocks: one scale per 128-row Q tile
+    const float qscale = !row_valid ? 0.f : QF8 ? p.qs[bh * p.nqs + qt] : p.qs[bh * p.nqs + (row >> 4) * 8 + (row & 7)];
     const float scale = p.sm_scale;
     const uint64_t bias2 = pk2f(kBias, kBias);
     const uint64_t tiny2 = pk2(kDenormOne, kDenormOne);
     const uint64_t expa2 = pk2f(kExpA, kExpA), expb2 = pk2f(kExpB, kExpB);
     mbar_arrive(&bar->s_free[w]);   // S[w] is free for this group's first tile
     bool ok = true;
-    float4 ksv_next = w < T ? __ldg(reinterpret_cast<const float4*>(p.ks + bh * p.nks + w * 4)) : make_float4(1, 1, 1, 1);
+    // K scales of a tile: INT8 four groups (index tile*4 + (key%8)/2); E4M3 blocks one scale per kq_tiles tiles
+    auto load_ks = [&](int jj) -> float4 {
+      if constexpr (QF8) {
+        const float v = __ldg(p.ks + bh * p.nks + jj / p.kq_tiles);
+        return make_float4(v, v, v, v);
+      } else {
+        return __ldg(reinterpret_cast<const float4*>(p.ks + bh * p.nks + jj * 4));
+      }
+    };
+    float4 ksv_next = w < T ? load_ks(w) : make_float4(1, 1, 1, 1);
     for (int j = w; j < T; j += 2) {
       const int b = j & 1;   // == w
       const float4 ksv = ksv_next;
-      if (j + 2 < T) ksv_next = __ldg(reinterpret_cast<const float4*>(p.ks + bh * p.nks + (j + 2) * 4));
+      if (j + 2 < T) ksv_next = load_ks(j + 2);
       const uint32_t scol = tmem + lane_base + (b ? kAColS1 : kAColS0);
       ok = mbar_wait_warp(&bar->s_full[b], (j >> 1) & 1, kErrTimeoutSoftmax);
       if (!ok) break;
@@ -401,7 +419,11 @@ __global__ void __launch_bounds__(kAltThreads, 1)
 #pragma unroll
         for (int k = 2; k < 16; ++k)
           mx = max3f(mx, __uint_as_float(raw[8 * k + 2 * g]), __uint_as_float(raw[8 * k + 2 * g + 1]));
-        if (mx > 0.f) lmax = fmaxf(lmax, __fmul_rn(__fsub_rn(mx, kBias), f1[g]));
+        if constexpr (QF8) {
+          if (mx > -__int_as_float(0x7f800000)) lmax = fmaxf(lmax, __fmul_rn(mx, f1[g]));
+        } else {
+          if (mx > 0.f) lmax = fmaxf(lmax, __fmul_rn(__fsub_rn(mx, kBias), f1[g]));
+        }
       }
       // running maximum handed over from the other group's previous tile
       float mprev = -5000000.0f;
@@ -435,7 +457,8 @@ __global__ void __launch_bounds__(kAltThreads, 1)
             const int c = 4 * wd + 2 * q2;
             const int g = (c >> 1) & 3;
             // u = fma(float(raw), RN(f A), fma(-m, A, B)) (the folded affine encoder)
-            const uint64_t u2 = f2_fma(f2_sub(pk2(raw[c], raw[c + 1]), bias2), gain2[g], cb2);
+            const uint64_t x2 = QF8 ? pk2(raw[c], raw[c + 1]) : f2_sub(pk2(raw[c], raw[c + 1]), bias2);
+            const uint64_t u2 = f2_fma(x2, gain2[g], cb2);
             up2(f2_mul(u2, tiny2), e[2 * q2], e[2 * q2 + 1]);
           }
           pw[wd] = pack_u8x2(e[1], e[0], pack_u8x2(e[3], e[2], 0u));
@@ -450,7 +473,8 @@ __global__ void __launch_bounds__(kAltThreads, 1)
             const int c = 4 * wd + 2 * q2;
             const int g = (c >> 1) & 3;
             // u = fma(RN(RN(float(raw) f) - m), A, B) (the unfused contract)
-            const uint64_t sh = f2_sub(f2_mul(f2_sub(pk2(raw[c], raw[c + 1]), bias2), pk2f(f1[g], f1[g])), m2);
+            const uint64_t x2 = QF8 ? pk2(raw[c], raw[c + 1]) : f2_sub(pk2(raw[c], raw[c + 1]), bias2);
+            const uint64_t sh = f2_sub(f2_mul(x2, pk2f(f1[g], f1[g])), m2);
             up2(f2_mul(f2_fma(sh, expa2, expb2), tiny2), e[2 * q2], e[2 * q2 + 1]);
           }
           pw[wd] = pack_u8x2(e[1], e[0], pack_u8x2(e[3], e[2], 0u));

@@ -150,11 +150,12 @@ int vc_error_read(int device, uint32_t* code, int clear) {
     set_last_error("vc_error_read: bad device %d", device);
     return VC_ERR_ARG;
   }
-  uint32_t words[3] = {0, 0, 0};
+  uint32_t words[4] = {0, 0, 0, 0};
   cudaError_t e = attention_error_word(&words[0], clear != 0);
   if (e == cudaSuccess) e = prep_qk_error_word(&words[1], clear != 0);
   if (e == cudaSuccess) e = prep_v_error_word(&words[2], clear != 0);
-  *code = words[0] | words[1] | words[2];
+  if (e == cudaSuccess) e = prep_hadamard_error_word(&words[3], clear != 0);
+  *code = words[0] | words[1] | words[2] | words[3];
   cudaSetDevice(prev);
   if (e != cudaSuccess) {
     set_last_error("vc_error_read: %s", cudaGetErrorString(e));
@@ -198,6 +199,43 @@ int vc_prep_qk_int8(const void* q, const void* k, int dtype, int64_t B, int64_t 
   PrepQKArgs a{q, k, dtype, B, H, Sq, Sk, D, q_stride_b, q_stride_h, q_stride_s, k_stride_b, k_stride_h, k_stride_s,
                perm, km_in, km_out, mean_numel_out, mean_numel_in, q8, qs, k8, ks, workspace};
   return finish(fn, prep_qk(a, static_cast<cudaStream_t>(stream)));
+}
+
+int64_t vc_prep_qk_hadamard_workspace_bytes(int64_t B, int64_t H, int64_t Sq, int64_t Sk, int64_t D,
+                                            int64_t k_quant_block) {
+  if (k_quant_block < 128 || k_quant_block % 128 || k_quant_block > 4096) return -1;
+  return prep_hadamard_workspace(B, H, Sq, Sk, D, k_quant_block);
+}
+
+int vc_prep_qk_hadamard_e4m3(const void* q, const void* k, int dtype, int64_t B, int64_t H, int64_t Sq, int64_t Sk,
+                             int64_t D, int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
+                             int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s, const int64_t* perm,
+                             int k_smooth, const float* km_in, float* km_out, int64_t k_quant_block, uint8_t* q8,
+                             float* qs, uint8_t* k8, float* ks, void* workspace, int64_t workspace_bytes,
+                             void* stream) {
+  const char* fn = "vc_prep_qk_hadamard_e4m3";
+  if (int rc = check_common(fn, dtype, B, H, Sq, D)) return rc;
+  if (int rc = check_common(fn, dtype, B, H, Sk, D)) return rc;
+  if (int rc = check_input(fn, "q", q, dtype, q_stride_b, q_stride_h, q_stride_s)) return rc;
+  if (int rc = check_input(fn, "k", k, dtype, k_stride_b, k_stride_h, k_stride_s)) return rc;
+  if (k_quant_block < 128 || k_quant_block % 128 || k_quant_block > 4096) {
+    set_last_error("%s: k_quant_block must be a multiple of 128 in [128, 4096] (got %lld)", fn,
+                   (long long)k_quant_block);
+    return VC_ERR_ARG;
+  }
+  if (!q8 || !k8 || !qs || !ks || !aligned16(q8) || !aligned16(k8)) {
+    set_last_error("%s: q8/k8/qs/ks must be non-null and q8/k8 16-byte aligned", fn);
+    return VC_ERR_ARG;
+  }
+  const int64_t need = prep_hadamard_workspace(B, H, Sq, Sk, D, k_quant_block);
+  if (!workspace || workspace_bytes < need || !aligned16(workspace)) {
+    set_last_error("%s: workspace needs %lld bytes (16-byte aligned)", fn, (long long)need);
+    return VC_ERR_WORKSPACE;
+  }
+  if (int rc = check_device()) return rc;
+  PrepHadArgs a{q, k, dtype, B, H, Sq, Sk, D, q_stride_b, q_stride_h, q_stride_s, k_stride_b, k_stride_h, k_stride_s,
+                perm, k_smooth ? 1 : 0, km_in, km_out, k_quant_block, q8, qs, k8, ks, workspace};
+  return finish(fn, prep_hadamard(a, static_cast<cudaStream_t>(stream)));
 }
 
 int64_t vc_prep_v_channel_workspace_bytes(int64_t B, int64_t H, int64_t S, int64_t D) {
@@ -332,6 +370,44 @@ int vc_attention_fwd(const int8_t* q8, const float* qs, const int8_t* k8, const 
   AttnArgs a{q8, qs, k8, ks, v8, vs, means, out, out_dtype, B, H, Sq, Sk, D, out_stride_b, out_stride_h, out_stride_s,
              expcast == 2 ? 2 : (expcast ? 1 : 0), block_values ? 1 : 0, vs_per_block ? 1 : 0, sm_scale, unit_begin,
              unit_end};
+  return finish(fn, attention_fwd(a, static_cast<cudaStream_t>(stream)));
+}
+
+int vc_attention_fwd_e4m3qk(const uint8_t* q8, const float* qs, const uint8_t* k8, const float* ks,
+                            const uint8_t* v8, const float* vs, const uint16_t* means, void* out, int out_dtype,
+                            int64_t B, int64_t H, int64_t Sq, int64_t Sk, int64_t D, int64_t out_stride_b,
+                            int64_t out_stride_h, int64_t out_stride_s, int expcast, int block_values,
+                            int64_t k_quant_block, float sm_scale, int64_t unit_begin, int64_t unit_end,
+                            void* stream) {
+  const char* fn = "vc_attention_fwd_e4m3qk";
+  if (int rc = check_common(fn, VC_DTYPE_BF16, B, H, Sq, D)) return rc;
+  if (int rc = check_common(fn, VC_DTYPE_BF16, B, H, Sk, D)) return rc;
+  if (out_dtype != VC_DTYPE_F16 && out_dtype != VC_DTYPE_BF16 && out_dtype != VC_DTYPE_F32) {
+    set_last_error("%s: out_dtype must be F16, BF16 or F32", fn);
+    return VC_ERR_ARG;
+  }
+  if (!q8 || !qs || !k8 || !ks || !v8 || !vs || !out || (block_values && !means) || !aligned16(q8) ||
+      !aligned16(k8) || !aligned16(v8) || !aligned16(vs) || (block_values && !aligned16(means))) {
+    set_last_error("%s: payload pointers must be non-null and q8/k8/v8/vs/means 16-byte aligned", fn);
+    return VC_ERR_ARG;
+  }
+  if (check_input(fn, "out", out, out_dtype, out_stride_b, out_stride_h, out_stride_s)) return VC_ERR_ARG;
+  if (expcast != 1 && expcast != 2) {
+    set_last_error("%s: the E4M3 Q/K kernel runs ExpCast only (expcast 1 or 2)", fn);
+    return VC_ERR_UNSUPPORTED;
+  }
+  if (k_quant_block < 128 || k_quant_block % 128 || k_quant_block > 4096) {
+    set_last_error("%s: k_quant_block must be a multiple of 128 in [128, 4096]", fn);
+    return VC_ERR_ARG;
+  }
+  if (!(sm_scale > 0.f) || !(sm_scale <= 3.4028234663852886e38f)) {
+    set_last_error("%s: sm_scale must be positive and finite", fn);
+    return VC_ERR_ARG;
+  }
+  if (int rc = check_device()) return rc;
+  AttnArgs a{reinterpret_cast<const int8_t*>(q8), qs, reinterpret_cast<const int8_t*>(k8), ks, v8, vs, means, out,
+             out_dtype, B, H, Sq, Sk, D, out_stride_b, out_stride_h, out_stride_s, expcast, block_values ? 1 : 0, 0,
+             sm_scale, unit_begin, unit_end, 1, k_quant_block};
   return finish(fn, attention_fwd(a, static_cast<cudaStream_t>(stream)));
 }
 

@@ -25,6 +25,27 @@ struct PrepQKArgs {
 int64_t prep_qk_workspace(int64_t B, int64_t H, int64_t Sk, int64_t D);
 int prep_qk(const PrepQKArgs& a, cudaStream_t st);
 
+struct PrepHadArgs {
+  const void* q;
+  const void* k;
+  int dtype;
+  int64_t B, H, Sq, Sk, D;
+  int64_t qsb, qsh, qss, ksb, ksh, kss;
+  const int64_t* perm;
+  int k_smooth;
+  const float* km_in;   // [B*H][D] FP32 or null (computed)
+  float* km_out;        // optional
+  int64_t kqb;          // K rows per scale block (a multiple of 128)
+  uint8_t* q8;
+  float* qs;
+  uint8_t* k8;
+  float* ks;
+  void* workspace;
+};
+int64_t prep_hadamard_workspace(int64_t B, int64_t H, int64_t Sq, int64_t Sk, int64_t D, int64_t kqb);
+int prep_hadamard(const PrepHadArgs& a, cudaStream_t st);
+cudaError_t prep_hadamard_error_word(uint32_t* code, bool clear);
+
 struct PrepVArgs {
   const void* v;
   int dtype;
@@ -73,6 +94,8 @@ struct AttnArgs {
   int expcast, block_values, vs_per_block;
   float sm_scale;
   int64_t unit_begin, unit_end;
+  int qk_e4m3;        // 1: E4M3 block Q/K payloads (qs per 128-row Q tile, ks per kqb K rows)
+  int64_t kqb;
 };
 int attention_fwd(const AttnArgs& a, cudaStream_t st);
 // Copy (and optionally clear) the device error word of each kernel file on the

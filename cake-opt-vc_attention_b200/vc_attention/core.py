@@ -6,16 +6,21 @@ total_steps, request_id, layer_id, scale, causal, mask) -> (output,
 counters)`` -- (src/vc_attention/core.py:15-371, __init__.py) and adds
 ``backend="sm100a"``.
 
-The sm100a backend runs this repository's INT8 ``sageattn_vc`` pipeline on
-the GPU: Sage per-thread INT8 Q/K after K channel-mean centring
-(``k_smooth``), ExpCast E4M3 probabilities (``expcast``), per-channel E4M3 V,
-and -- while smoothing is active -- V grouping with 128-token block means.
-That is the contract the reference's Config numerics are compared against
-within a tolerance, not byte for byte: the reference backends quantise Q/K
-as E4M3 blocks after an optional Hadamard rotation (core.py:79-107), which
-this backend does not implement, so ``qk_hadamard=True`` is rejected.  The
-reference's own backends ("reference", "npu_fp8", "cuda_fp8") are accepted by
-``Config`` for compatibility but not executed here: there is no CPU path.
+The sm100a backend runs on the GPU with ExpCast E4M3 probabilities
+(``expcast``), per-channel E4M3 V and -- while smoothing is active -- V
+grouping with 128-token block means.  Its Q/K format follows
+``qk_hadamard``:
+  * ``qk_hadamard=True`` (the Config contract's own path, core.py:79-107,
+    128-150): K centred by its FP32 channel mean (``k_smooth``), Q and K
+    rotated by the normalised Sylvester transform, E4M3 block payloads with
+    one scale per ``q_block`` = 128 Q rows and per ``k_quant_block`` K rows,
+    QK^T on the FP8 tensor cores.  ExpCast only.
+  * ``qk_hadamard=False``: this repository's INT8 ``sageattn_vc`` pipeline
+    (Sage per-thread INT8 Q/K after K channel-mean centring).
+Both are compared with the reference backend within a tolerance, not byte
+for byte (V is quantised per channel here, per tile there).  The reference's
+own backends ("reference", "npu_fp8", "cuda_fp8") are accepted by ``Config``
+for compatibility but not executed here: there is no CPU path.
 """
 from __future__ import annotations
 
@@ -76,10 +81,13 @@ class Config:
                 raise ValueError("cuda_fp8 q_block/kv_block must be multiples of 32 in [32, 256]")
             if self.k_quant_block > 4096:
                 raise ValueError("cuda_fp8 k_quant_block must be <= 4096")
-        # sm100a: the INT8 sageattn_vc pipeline's fixed geometry
+        # sm100a: the fused kernel's fixed geometry
         if self.backend == "sm100a":
-            if self.qk_hadamard:
-                raise ValueError("sm100a runs INT8 Q/K without the Hadamard rotation; set qk_hadamard=False")
+            if self.qk_hadamard and not self.expcast:
+                raise ValueError("sm100a runs the Hadamard E4M3 Q/K path with ExpCast only; "
+                                 "set expcast=True, or qk_hadamard=False for the INT8 path")
+            if self.qk_hadamard and (self.k_quant_block % 128 or self.k_quant_block > 4096):
+                raise ValueError("sm100a requires k_quant_block to be a multiple of 128, at most 4096")
             if self.q_block != 128 or self.kv_block != 128:
                 raise ValueError("sm100a requires q_block=128 and kv_block=128")
             if self.v_smooth and self.clusters > 8:

@@ -1,4 +1,5 @@
-"""sm100a backend of the Config API: the INT8 ``sageattn_vc`` pipeline.
+"""sm100a backend of the Config API: the Hadamard E4M3 block Q/K path
+(``qk_hadamard=True``) or the INT8 ``sageattn_vc`` pipeline.
 
 Plays the role of the reference's cuda_backend.py:37-88 (``_attention``):
 validate the device, apply the request's V layout, prepare payloads and run
@@ -55,15 +56,19 @@ def attention(q, k, v, cfg, *, cache, step, total_steps, request_id, layer_id, s
         pi, active, refreshed = cache.layout(v, step=step, total_steps=total_steps, request_id=request_id,
                                              layer_id=layer_id)
         B, H, _, D = k.shape
-        km = None if cfg.k_smooth else torch.zeros((B, H, 1, D), dtype=k.dtype, device=k.device)
-        q8, qs, k8, ks, _ = ops.prep_qk_int8(q, k, perm=pi, km=km)
+        if cfg.qk_hadamard:
+            q8, qs, k8, ks, _ = ops.prep_qk_hadamard(q, k, perm=pi, k_smooth=cfg.k_smooth,
+                                                     k_quant_block=cfg.k_quant_block)
+        else:
+            km = None if cfg.k_smooth else torch.zeros((B, H, 1, D), dtype=k.dtype, device=k.device)
+            q8, qs, k8, ks, _ = ops.prep_qk_int8(q, k, perm=pi, km=km)
         if active:
             v8, vs, means = ops.prep_v_blocks(v, perm=pi, channel_scale=True)
         else:
             v8, vs = ops.prep_v_channel(v, perm=pi)
             means = None
         out = ops.attention_fwd(q8, qs, k8, ks, v8, vs, means, out_dtype=q.dtype, sm_scale=float(scale),
-                                expcast=cfg.expcast, block_values=active)
+                                expcast=cfg.expcast, block_values=active, k_quant_block=cfg.k_quant_block)
     tiles = math.ceil(q.shape[-2] / 128) * math.ceil(k.shape[-2] / 128)
     return out, {
         "backend": "sm100a",
@@ -77,7 +82,7 @@ def attention(q, k, v, cfg, *, cache, step, total_steps, request_id, layer_id, s
         "native_fused_attention": True,
         "preprocessing_fused": False,
         "native_fp8_matmul": True,
-        "native_int8_matmul": True,
+        "native_int8_matmul": not cfg.qk_hadamard,
         "cuda_schedule": "fused",
         "cuda_fused_pipeline": True,
         "cuda_fused_variant": "sm100a_tcgen05",

@@ -27,6 +27,9 @@ SIGNATURES = {
     "vc_prep_qk_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64]),
     "vc_prep_qk_int8": (_i32, [_p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                _p, _p, _p, _i64, _i64, _p, _p, _p, _p, _p, _i64, _p]),
+    "vc_prep_qk_hadamard_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64, _i64, _i64]),
+    "vc_prep_qk_hadamard_e4m3": (_i32, [_p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                                        _i64, _p, _i32, _p, _p, _i64, _p, _p, _p, _p, _p, _i64, _p]),
     "vc_prep_v_channel_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64]),
     "vc_prep_v_channel": (_i32, [_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _p]),
     "vc_prep_v_channel_static": (_i32, [_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p]),
@@ -38,6 +41,8 @@ SIGNATURES = {
                                _i64, _p]),
     "vc_attention_fwd": (_i32, [_p, _p, _p, _p, _p, _p, _p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                 _i32, _i32, _i32, _f, _i64, _i64, _p]),
+    "vc_attention_fwd_e4m3qk": (_i32, [_p, _p, _p, _p, _p, _p, _p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                                       _i64, _i32, _i32, _i64, _f, _i64, _i64, _p]),
     "vc_kernel_resources": (_i32, [_i32, C.POINTER(C.c_int64)]),
 }
 

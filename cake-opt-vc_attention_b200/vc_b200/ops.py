@@ -101,6 +101,47 @@ def prep_qk_int8(q: torch.Tensor, k: torch.Tensor, *, perm: torch.Tensor | None 
     return q8, qs, k8, ks, km_out
 
 
+def prep_qk_hadamard(q: torch.Tensor, k: torch.Tensor, *, perm: torch.Tensor | None = None, k_smooth: bool = True,
+                     k_quant_block: int = 256, km: torch.Tensor | None = None):
+    """The Config contract's own Q/K format (qk_hadamard=True): K centred by
+    its FP32 channel mean (``k_smooth``), Q and K rotated by the normalised
+    Sylvester transform, E4M3 block payloads with one scale per 128 Q rows
+    and per ``k_quant_block`` K rows (HND inputs).
+
+    Returns (q8, qs, k8, ks, km): q8/k8 float8_e4m3fn [B,H,S,D] (k8 rows in
+    permutation order), qs [B,H,ceil(Sq/128)], ks [B,H,ceil(Sk/k_quant_block)]
+    FP32, km [B,H,D] FP32 (None without ``k_smooth``).  ``km`` is computed on
+    the device unless given.
+    """
+    _require_cuda("prep_qk_hadamard", q, k, perm, km)
+    q, k = _rowmajor(q), _rowmajor(k)
+    B, H, Sq, D = q.shape
+    Sk = k.shape[2]
+    if k.shape[:2] != (B, H) or k.shape[3] != D:
+        raise ValueError("Q/K batch, heads and head dim must match")
+    dev = q.device
+    q8 = torch.empty((B, H, Sq, D), dtype=torch.float8_e4m3fn, device=dev)
+    k8 = torch.empty((B, H, Sk, D), dtype=torch.float8_e4m3fn, device=dev)
+    kqb = int(k_quant_block)
+    qs = torch.empty((B, H, (Sq + 127) // 128), dtype=torch.float32, device=dev)
+    ks = torch.empty((B, H, max(1, (Sk + kqb - 1) // max(kqb, 1))), dtype=torch.float32, device=dev)
+    km_in = None if km is None else km.reshape(B, H, D).to(torch.float32).contiguous()
+    km_out = torch.empty((B, H, D), dtype=torch.float32, device=dev) if k_smooth else None
+    perm = _perm("prep_qk_hadamard", perm, B, H, Sk)
+    lib = N.load()
+    wsb = lib.vc_prep_qk_hadamard_workspace_bytes(B, H, Sq, Sk, D, kqb)
+    if wsb < 0:
+        raise ValueError("k_quant_block must be a multiple of 128 in [128, 4096]")
+    ws = _workspace(wsb, dev)
+    with torch.cuda.device(dev):
+        N.check(lib.vc_prep_qk_hadamard_e4m3(_p(q), _p(k), _DT[q.dtype], B, H, Sq, Sk, D, q.stride(0), q.stride(1),
+                                             q.stride(2), k.stride(0), k.stride(1), k.stride(2), _p(perm),
+                                             int(bool(k_smooth)), _p(km_in), _p(km_out), kqb, _p(q8), _p(qs),
+                                             _p(k8), _p(ks), _p(ws), ws.numel(), _stream(q)),
+                "vc_prep_qk_hadamard_e4m3")
+    return q8, qs, k8, ks, km_out
+
+
 def prep_v_channel(v: torch.Tensor, *, perm: torch.Tensor | None = None):
     """Unsmoothed per-channel E4M3 V: (v8 [B,H,D,Npad] float8_e4m3fn, vs [B,H,D])."""
     _require_cuda("prep_v_channel", v, perm)
@@ -171,7 +212,7 @@ def group_values(v: torch.Tensor, clusters: int = 8, iterations: int = 2, *, cen
 
 def attention_fwd(q8, qs, k8, ks, v8, vs, means, *, out_dtype=torch.bfloat16, sm_scale: float | None = None,
                   expcast: bool = True, block_values: bool = False, out: torch.Tensor | None = None,
-                  unit_range: tuple[int, int] | None = None) -> torch.Tensor:
+                  unit_range: tuple[int, int] | None = None, k_quant_block: int = 256) -> torch.Tensor:
     """Fused attention on prepared payloads.  Returns ``out`` [B,H,Sq,D].
 
     ``expcast``: True = ExpCast with the reference's folded affine encoder
@@ -180,6 +221,10 @@ def attention_fwd(q8, qs, k8, ks, v8, vs, means, *, out_dtype=torch.bfloat16, sm
 
     ``unit_range`` = [begin, end) over units (b*H+h)*ceil(Sq/128)+q_tile
     computes only that shard (rows outside it are left untouched).
+
+    Q/K payloads from ``prep_qk_hadamard`` (float8_e4m3fn) select the E4M3
+    block-QK kernel; ``k_quant_block`` is then their K scale block (ExpCast
+    and per-channel V scales only).
     """
     _require_cuda("attention_fwd", q8, k8, v8)
     B, H, Sq, D = q8.shape
@@ -194,6 +239,18 @@ def attention_fwd(q8, qs, k8, ks, v8, vs, means, *, out_dtype=torch.bfloat16, sm
     vs_per_block = bool(block_values and vs.dim() == 4)
     ub, ue = unit_range if unit_range is not None else (0, -1)
     lib = N.load()
+    if q8.dtype == torch.float8_e4m3fn:
+        if k8.dtype != torch.float8_e4m3fn:
+            raise ValueError("E4M3 Q needs E4M3 K payloads")
+        if not expcast or vs_per_block:
+            raise ValueError("the E4M3 block-QK kernel runs ExpCast with per-channel V scales only")
+        with torch.cuda.device(q8.device):
+            N.check(lib.vc_attention_fwd_e4m3qk(_p(q8), _p(qs), _p(k8), _p(ks), _p(v8.view(torch.uint8)), _p(vs),
+                                                _p(means) if block_values else None, _p(out), _DT[out.dtype], B, H,
+                                                Sq, Sk, D, out.stride(0), out.stride(1), out.stride(2),
+                                                2 if expcast == "exact" else 1, int(block_values), int(k_quant_block),
+                                                scale, int(ub), int(ue), _stream(q8)), "vc_attention_fwd_e4m3qk")
+        return out
     with torch.cuda.device(q8.device):
         N.check(lib.vc_attention_fwd(_p(q8), _p(qs), _p(k8), _p(ks), _p(v8.view(torch.uint8)), _p(vs),
                                      _p(means) if block_values else None, _p(out), _DT[out.dtype], B, H, Sq, Sk, D,

@@ -81,6 +81,27 @@ int vc_prep_qk_int8(const void* q, const void* k, int dtype, int64_t B, int64_t 
                     int64_t mean_numel_out, int64_t mean_numel_in, int8_t* q8, float* qs, int8_t* k8, float* ks,
                     void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Q/K for the Config contract's own QK path (qk_hadamard=True): K centred by
+ * its FP32 channel mean over all tokens when k_smooth (km_in [B*H][D] FP32 if
+ * given, else computed; written to km_out when non-null), Q and K rotated by
+ * the normalised Sylvester transform on channels, then E4M3 block payloads:
+ * q8 [B,H,Sq,D] with qs [B,H,ceil(Sq/128)] (q_block 128) and k8 [B,H,Sk,D]
+ * (rows in permutation order when perm is given) with ks
+ * [B,H,ceil(Sk/k_quant_block)]; scale = amax/448 (1 for an all-zero block),
+ * payload = e4m3_rn_satfinite(x / scale).  k_quant_block must be a positive
+ * multiple of 128 (at most 4096).
+ * Replaces core.py:79-107 (hadamard, preprocess_qk) and :128-150 (_encode,
+ * _quantize_qk) of src/vc_attention, the cuda_fp8 backend's Q/K preparation
+ * (csrc/kernels.cu:104-152). */
+int64_t vc_prep_qk_hadamard_workspace_bytes(int64_t B, int64_t H, int64_t Sq, int64_t Sk, int64_t D,
+                                            int64_t k_quant_block);
+int vc_prep_qk_hadamard_e4m3(const void* q, const void* k, int dtype, int64_t B, int64_t H, int64_t Sq, int64_t Sk,
+                             int64_t D, int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
+                             int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s, const int64_t* perm,
+                             int k_smooth, const float* km_in, float* km_out, int64_t k_quant_block, uint8_t* q8,
+                             float* qs, uint8_t* k8, float* ks, void* workspace, int64_t workspace_bytes,
+                             void* stream);
+
 /* Unsmoothed V: per-channel E4M3 (scale = amax/448, payload = e4m3(x*448/amax);
  * all-zero channels get scale 0 and payload 0).
  * Replaces vc.py:162-166 -> quant.py:223-292 per_channel_fp8(smooth_v=False)
@@ -154,6 +175,20 @@ int vc_attention_fwd(const int8_t* q8, const float* qs, const int8_t* k8, const 
                      int64_t Sq, int64_t Sk, int64_t D, int64_t out_stride_b, int64_t out_stride_h,
                      int64_t out_stride_s, int expcast, int block_values, int vs_per_block, float sm_scale,
                      int64_t unit_begin, int64_t unit_end, void* stream);
+
+/* vc_attention_fwd with E4M3 block Q/K payloads (vc_prep_qk_hadamard_e4m3):
+ * QK^T is a tcgen05 kind::f8f6f4 MMA into FP32 and the logits are
+ * raw * (sm_scale * (qs[q_tile] * ks[key / k_quant_block])).  ExpCast only
+ * (expcast 1 or 2) with per-channel V scales (vs_per_block = 0); other
+ * arguments as vc_attention_fwd.
+ * Replaces the cuda_fp8 backend's fused attention on its E4M3 block Q/K
+ * (src/vc_attention/cuda_backend.py:37-88, core.py:335-345 semantics). */
+int vc_attention_fwd_e4m3qk(const uint8_t* q8, const float* qs, const uint8_t* k8, const float* ks,
+                            const uint8_t* v8, const float* vs, const uint16_t* means, void* out, int out_dtype,
+                            int64_t B, int64_t H, int64_t Sq, int64_t Sk, int64_t D, int64_t out_stride_b,
+                            int64_t out_stride_h, int64_t out_stride_s, int expcast, int block_values,
+                            int64_t k_quant_block, float sm_scale, int64_t unit_begin, int64_t unit_end,
+                            void* stream);
 
 /* Compiled resources of the fused kernel (registers/thread, static+dynamic
  * shared bytes, threads) for head_dim 64/128 into out[0..3].

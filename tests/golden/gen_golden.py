@@ -50,8 +50,17 @@ def sage_state(st):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("VC_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--hadamard", action="store_true",
+                    help="only (re)write the Hadamard / E4M3 block-QK fixtures (step 5)")
     args = ap.parse_args()
     ref = Path(args.reference)
+    if args.hadamard:
+        sys.path.insert(0, str(ref / "src"))
+        from vc_attention import core
+        manifest = json.loads((HERE / "manifest.json").read_text())
+        hadamard_fixtures(core, manifest)
+        (HERE / "manifest.json").write_text(json.dumps(manifest, indent=1, default=str) + "\n")
+        return
     sage = ref / "third_party/sageattention_local/sageattention_local"
     vc_ref = load(sage / "vc_reference.py", "ref_vc_reference")
     qpt = load(sage / "triton/quant_per_thread.py", "ref_quant_per_thread")
@@ -121,8 +130,44 @@ def main():
                             config=json.dumps(kw))
         manifest[name] = {"shape": list(shape), "config": kw, "counters": {k2: v2 for k2, v2 in counters.items()}}
 
+    hadamard_fixtures(core, manifest)
     (HERE / "manifest.json").write_text(json.dumps(manifest, indent=1, default=str) + "\n")
     print(json.dumps(manifest, indent=1, default=str))
+
+
+def hadamard_fixtures(core, manifest):
+    """5. The Config contract's own QK path (qk_hadamard=True): Q/K payloads
+    from the reference's preprocess_qk + _encode per block, and reference
+    backend outputs of core.attention."""
+    cases = {"hadamard_qk": (21, (1, 2, 300, 128), torch.bfloat16, 2 ** 0.5, 256),
+             "hadamard_qk_d64": (22, (2, 1, 517, 64), torch.float16, 1.0, 128)}
+    for name, (seed, shape, dtype, koff, kqb) in cases.items():
+        q, k, _ = qk_inputs(seed, shape, dtype, koff)
+        km = k.float().mean(dim=-2)
+        qh, kh = core.preprocess_qk(q, k, k_smooth=True, qk_hadamard=True)
+        out = {}
+        for tag, x, block in (("q", qh, 128), ("k", kh, kqb)):
+            bits, scales = [], []
+            for start in range(0, x.shape[-2], block):
+                payload, scale = core._encode(x[..., start:start + block, :], (-2, -1))
+                bits.append(payload.view(torch.uint8))
+                scales.append(scale.reshape(*x.shape[:-2], 1))
+            out[tag + "8"] = torch.cat(bits, dim=-2).numpy()
+            out[tag + "s"] = torch.cat(scales, dim=-1).numpy()
+        np.savez_compressed(HERE / f"{name}.npz", seed=seed, shape=shape, koff=koff, dtype=str(dtype).split(".")[-1],
+                            k_quant_block=kqb, km=km.numpy(), **out)
+        manifest[name] = {"shape": list(shape), "dtype": str(dtype), "k_quant_block": kqb}
+    cfg_cases = {
+        "cfg_hadamard": (23, (1, 2, 640, 128), torch.float32, 2 ** 0.5, dict(expcast=True, qk_hadamard=True)),
+        "cfg_hadamard_smooth": (24, (1, 2, 500, 64), torch.float32, 1.0,
+                                dict(expcast=True, v_smooth=True, qk_hadamard=True, k_quant_block=128)),
+    }
+    for name, (seed, shape, dtype, koff, kw) in cfg_cases.items():
+        q, k, v = qk_inputs(seed, shape, dtype, koff)
+        out, counters = core.attention(q, k, v, core.Config(backend="reference", **kw))
+        np.savez_compressed(HERE / f"{name}.npz", seed=seed, shape=shape, koff=koff, out=out.numpy(),
+                            config=json.dumps(kw))
+        manifest[name] = {"shape": list(shape), "config": kw, "counters": {k2: v2 for k2, v2 in counters.items()}}
 
 
 if __name__ == "__main__":

@@ -530,3 +530,91 @@ def test_sharded_host_pipeline_equals_device_shards(ops, smooth):
         assert torch.isnan(got[:r0].float()).all() and torch.isnan(got[r1:].float()).all()
         covered[r0:r1] = True
     assert covered.all()
+
+
+# --- the Config contract's own Q/K path: Hadamard rotation + E4M3 blocks ---------------------------
+
+@pytest.mark.parametrize("name", ["hadamard_qk", "hadamard_qk_d64"])
+def test_hadamard_prep_matches_reference_payloads(ops, name):
+    """Device Hadamard + E4M3 block preparation against payloads and scales
+    written by the reference's preprocess_qk + _encode: bit for bit given its
+    FP32 K mean.  The K mean computed on the device (fixed-order FP32 sums)
+    agrees with torch's to within rounding."""
+    f = np.load(GOLDEN / f"{name}.npz")
+    shape = tuple(int(x) for x in f["shape"])
+    q, k, _ = qk_inputs(int(f["seed"]), shape, getattr(torch, str(f["dtype"])), float(f["koff"]))
+    kqb = int(f["k_quant_block"])
+    q8, qs, k8, ks, km = ops.prep_qk_hadamard(q.cuda(), k.cuda(), k_smooth=True, k_quant_block=kqb,
+                                              km=torch.from_numpy(f["km"]).cuda())
+    assert q8.dtype == torch.float8_e4m3fn and k8.dtype == torch.float8_e4m3fn
+    assert np.array_equal(_np(q8.view(torch.uint8)), f["q8"]) and np.array_equal(_np(qs), f["qs"])
+    assert np.array_equal(_np(k8.view(torch.uint8)), f["k8"]) and np.array_equal(_np(ks), f["ks"])
+    *_, km_dev = ops.prep_qk_hadamard(q.cuda(), k.cuda(), k_smooth=True, k_quant_block=kqb)
+    assert torch.allclose(km_dev.cpu(), torch.from_numpy(f["km"]), rtol=1e-5, atol=1e-6)
+    assert ops.error_word(0, clear=True) == 0
+
+
+HAD_CASES = [
+    # shape, dtype, koff, k_quant_block, k_smooth, grouped (permutation + block means)
+    ((1, 2, 1000, 128), torch.bfloat16, 2 ** 0.5, 256, True, False),
+    ((2, 1, 333, 64), torch.float16, 1.0, 128, True, False),
+    ((1, 1, 129, 128), torch.float32, 3 ** 0.5, 512, False, False),
+    ((1, 2, 700, 128), torch.bfloat16, 1.0, 256, True, True),
+    ((1, 1, 1100, 64), torch.bfloat16, 2 ** 0.5, 384, True, True),
+]
+
+
+@pytest.mark.parametrize("shape,dtype,koff,kqb,k_smooth,grouped", HAD_CASES)
+def test_hadamard_attention_matches_oracle(ops, shape, dtype, koff, kqb, k_smooth, grouped):
+    """E4M3 block Q/K: the device payloads equal the oracle's (given the
+    device K mean, with the K permutation when grouped) and the FP8-QK
+    attention kernel meets the parity tolerance against the oracle on the
+    same payloads, with and without block means; bitwise repeatable."""
+    q, k, _ = qk_inputs(41, shape, dtype, koff)
+    v = mixture_values(41, shape, dtype) if grouped else torch.randn(shape, generator=torch.Generator().manual_seed(7)).to(dtype)
+    perm = ops.group_values(v.cuda(), 8, 2).cpu() if grouped else None
+    pc = perm.cuda() if grouped else None
+    q8, qs, k8, ks, km = ops.prep_qk_hadamard(q.cuda(), k.cuda(), perm=pc, k_smooth=k_smooth, k_quant_block=kqb)
+    ost = O.prepare_hadamard(q, k, k_smooth=k_smooth, k_quant_block=kqb,
+                             km=km.cpu() if km is not None else None, perm=perm)
+    assert np.array_equal(_np(q8.view(torch.uint8)), ost["q"]) and np.array_equal(_np(qs), ost["qs"])
+    assert np.array_equal(_np(k8.view(torch.uint8)), ost["k"]) and np.array_equal(_np(ks), ost["ks"])
+    if grouped:
+        v8, vs, means = ops.prep_v_blocks(v.cuda(), perm=pc, channel_scale=True)
+    else:
+        v8, vs = ops.prep_v_channel(v.cuda())
+        means = None
+    scale = shape[-1] ** -0.5
+    kw = dict(out_dtype=torch.float32, sm_scale=scale, block_values=grouped, k_quant_block=kqb)
+    out = ops.attention_fwd(q8, qs, k8, ks, v8, vs, means, **kw)
+    assert torch.equal(ops.attention_fwd(q8, qs, k8, ks, v8, vs, means, **kw), out)
+    state = {**ost, "v": _np(v8.view(torch.uint8)), "vs": vs.cpu(), "means": _np(means) if grouped else None,
+             "expcast": True, "block_values": grouped, "scale": scale}
+    m = O.metrics(out.cpu(), O.reference(state))
+    assert m["cos"] >= COS_MIN and m["rel_l2"] <= REL_MAX, m
+    assert ops.error_word(0, clear=True) == 0
+
+
+@pytest.mark.parametrize("name", ["cfg_hadamard", "cfg_hadamard_smooth"])
+def test_config_api_sm100a_hadamard_against_reference_backend(ops, name):
+    """Boundary A with qk_hadamard=True: the Config contract's own Q/K path
+    (Hadamard + E4M3 blocks, FP8 QK^T) against the reference package's
+    reference backend.  V is quantised per channel here and per tile there,
+    so this is a tolerance check, as for the INT8 path."""
+    from vc_attention import Config, attention
+    f = np.load(GOLDEN / f"{name}.npz")
+    kw = json.loads(str(f["config"]))
+    shape = tuple(int(x) for x in f["shape"])
+    q, k, v = qk_inputs(int(f["seed"]), shape, torch.float32, float(f["koff"]))
+    out, counters = attention(q.cuda(), k.cuda(), v.cuda(), Config(backend="sm100a", **kw))
+    ref = torch.from_numpy(f["out"])
+    m = O.metrics(out.cpu(), ref)
+    assert m["cos"] >= 0.998, m
+    dense = O.dense_attention(q, k, v)
+    ours, theirs = O.metrics(out.cpu(), dense), O.metrics(ref, dense)
+    assert ours["rel_l2"] <= 1.25 * theirs["rel_l2"] + 2e-3, (ours, theirs)
+    expected = json.loads((GOLDEN / "manifest.json").read_text())[name]["counters"]
+    for key in ("smoothing_active", "layout_refreshed", "expcast", "k_smooth", "qk_hadamard",
+                "numerical_contract_version", "tiles"):
+        assert counters[key] == expected[key], key
+    assert counters["qk_hadamard"] and not counters["native_int8_matmul"]

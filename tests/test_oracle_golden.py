@@ -241,3 +241,30 @@ def test_config_reference_fixture_within_band_of_oracle():
     out = O.reference(st)
     m = O.metrics(out, torch.from_numpy(f["out"]))
     assert m["rel_l2"] < 0.08 and m["cos"] > 0.995, m
+
+
+@pytest.mark.parametrize("name", ["hadamard_qk", "hadamard_qk_d64"])
+def test_hadamard_e4m3_blocks_match_reference(name):
+    """The oracle's Hadamard rotation and E4M3 block encoder (the Config
+    contract's own Q/K path) against payloads and scales written by the
+    reference's preprocess_qk + _encode, bit for bit, given its K mean."""
+    f = fixture(f"{name}.npz")
+    q, k, _ = qk_inputs(int(f["seed"]), tuple(int(x) for x in f["shape"]), getattr(torch, str(f["dtype"])),
+                        float(f["koff"]))
+    st = O.prepare_hadamard(q, k, k_smooth=True, k_quant_block=int(f["k_quant_block"]),
+                            km=torch.from_numpy(f["km"]))
+    assert np.array_equal(st["q"], f["q8"]) and np.array_equal(st["qs"], f["qs"])
+    assert np.array_equal(st["k"], f["k8"]) and np.array_equal(st["ks"], f["ks"])
+
+
+def test_hadamard_is_orthonormal_and_self_inverse():
+    """Known properties of the normalised Sylvester transform: norms kept and
+    H(H(x)) = x up to FP32 rounding; a one-hot row maps to +-1/sqrt(D)."""
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(50, 128, generator=g).numpy()
+    y = O.hadamard_fp32(x)
+    assert np.allclose(np.linalg.norm(y, axis=-1), np.linalg.norm(x, axis=-1), rtol=1e-5)
+    assert np.allclose(O.hadamard_fp32(y), x, atol=1e-5)
+    e = np.zeros((1, 64), np.float32)
+    e[0, 5] = 1
+    assert np.allclose(np.abs(O.hadamard_fp32(e)), 0.125)

@@ -36,6 +36,8 @@ def test_config_defaults_match_the_reference():
     ({"backend": "cuda_fp8", "quantize": False}, "quantize"),
     ({"backend": "cuda_fp8", "k_quant_block": 200}, "divide"),
     ({"backend": "sm100a"}, "qk_hadamard=False"),
+    ({"backend": "sm100a", "expcast": True, "k_quant_block": 200}, "multiple of 128"),
+    ({"backend": "sm100a", "expcast": True, "k_quant_block": 8192}, "multiple of 128"),
     ({"backend": "sm100a", "qk_hadamard": False, "quantize": False}, "quantize"),
     ({"backend": "sm100a", "qk_hadamard": False, "q_block": 64}, "q_block=128"),
     ({"backend": "sm100a", "qk_hadamard": False, "kv_block": 256, "k_quant_block": 256}, "kv_block=128"),
@@ -151,3 +153,12 @@ def test_layout_cache_contract_errors():
 def test_expcast_codes_has_no_cpu_path():
     with pytest.raises(ValueError, match="CUDA"):
         core.expcast_codes(torch.zeros(4))
+
+
+def test_sm100a_config_accepts_the_hadamard_path():
+    """qk_hadamard=True (the Config contract's E4M3 block Q/K) is accepted
+    with ExpCast and K scale blocks that are multiples of 128 rows."""
+    from vc_attention import Config
+    for kqb in (128, 256, 4096):
+        c = Config(backend="sm100a", expcast=True, qk_hadamard=True, k_quant_block=kqb)
+        assert c.qk_hadamard and c.k_quant_block == kqb
