@@ -618,3 +618,26 @@ def test_config_api_sm100a_hadamard_against_reference_backend(ops, name):
                 "numerical_contract_version", "tiles"):
         assert counters[key] == expected[key], key
     assert counters["qk_hadamard"] and not counters["native_int8_matmul"]
+
+
+def test_hadamard_attention_cross_lengths_and_shards(ops):
+    """E4M3 block Q/K with Sq != Sk against the oracle, and computed as three
+    unit ranges into one output: the same bits as one full call."""
+    g = torch.Generator().manual_seed(17)
+    q = torch.randn(1, 2, 300, 128, generator=g).to(torch.bfloat16)
+    k = (torch.randn(1, 2, 700, 128, generator=g) + torch.randn(1, 2, 1, 128, generator=g)).to(torch.bfloat16)
+    v = torch.randn(1, 2, 700, 128, generator=g).to(torch.bfloat16)
+    q8, qs, k8, ks, km = ops.prep_qk_hadamard(q.cuda(), k.cuda(), k_smooth=True, k_quant_block=256)
+    v8, vs = ops.prep_v_channel(v.cuda())
+    scale = 128 ** -0.5
+    full = ops.attention_fwd(q8, qs, k8, ks, v8, vs, None, out_dtype=torch.float32, sm_scale=scale)
+    ost = O.prepare_hadamard(q, k, k_smooth=True, k_quant_block=256, km=km.cpu())
+    state = {**ost, "v": _np(v8.view(torch.uint8)), "vs": vs.cpu(), "means": None, "expcast": True,
+             "block_values": False, "scale": scale}
+    m = O.metrics(full.cpu(), O.reference(state))
+    assert m["cos"] >= COS_MIN and m["rel_l2"] <= REL_MAX, m
+    out = torch.full_like(full, float("nan"))
+    units = 2 * 3   # (b*H + h) * ceil(300/128) + q_tile
+    for r in ((0, 2), (2, 5), (5, units)):
+        ops.attention_fwd(q8, qs, k8, ks, v8, vs, None, out=out, sm_scale=scale, unit_range=r)
+    assert torch.equal(out, full)
