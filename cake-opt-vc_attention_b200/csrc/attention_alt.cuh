@@ -29,6 +29,11 @@
 //                             row of E4M3 1.0 appended to every V tile
 //   P0 [400,432) P1 [432,464) ExpCast bytes of tiles j%2 (A operand of P.V)
 //   Q  [480,480+D/4)          int8 Q tile (A operand of Q.K^T)
+// QF8 (E4M3 block Q/K of the Config contract's Hadamard path): Q and K are
+// E4M3 bytes in the same layouts, QK^T is kind::f8f6f4 straight into FP32
+// (no preset, so the softmax reads plain FP32 scores and skips the bias
+// subtraction), and the scale factor of a tile is qs[q tile] * ks[key tile /
+// (k_quant_block/128)] for all its columns.
 // A group whose rows' maximum grew at tile j scales its lanes of O (and the
 // denominator column) after PV(j-1) completes and before it releases P(j).
 //
