@@ -223,16 +223,20 @@ __global__ void __launch_bounds__(kTileThreads) v_tile_quant(const T* __restrict
     }
     __syncthreads();
   }
-  // token pair t2 (rows 2t2, 2t2+1) x channel group of 8
+  // token pair t2 (rows 2t2, 2t2+1) x channel group of 8: each row's 8
+  // channels are contiguous in the staged tile, read as one vector
   constexpr int NG = D / 8;
   for (int i = threadIdx.x; i < 64 * NG; i += kTileThreads) {
     const int t2 = i % 64, g = i / 64;
     const int r0 = 2 * t2;
+    float xa[8], xb[8];
+    load_vec_smem<T, 8>(reinterpret_cast<const T*>(sin + r0 * G::kPitch + g * 8 * int(sizeof(T))), xa);
+    load_vec_smem<T, 8>(reinterpret_cast<const T*>(sin + (r0 + 1) * G::kPitch + g * 8 * int(sizeof(T))), xb);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int d = g * 8 + j;
-      float x0 = smem_elem<T>(sin, G::kPitch, r0, d);
-      float x1 = smem_elem<T>(sin, G::kPitch, r0 + 1, d);
+      float x0 = xa[j];
+      float x1 = xb[j];
       if constexpr (MODE == kPlainChannel) {
         x0 = __fmul_rn(x0, s_mul[d]);
         x1 = __fmul_rn(x1, s_mul[d]);
