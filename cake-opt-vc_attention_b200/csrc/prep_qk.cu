@@ -91,21 +91,19 @@ __device__ __forceinline__ float warp_max(float v) {
 //    q0 = RN(x*y) within one ulp of x/scale, the remainder
 //    r = fma(-q0, scale, x) is exact and RN(q0 + r*y) = RN(x/scale).
 //    Tiny quotients (|q| < 0.5) give 0 whatever their last bits.
-//  * trunc(RN(q + 0.5*sign q)) equals round-half-away-from-zero of q (the
-//    addition can only round when it crosses a power of two, which does not
-//    move the integer part): RNE via the 1.5*2^23 magic add, then ties
-//    (|q - RNE(q)| == 1/2) moved away from zero.  |q| <= 127.5 here.
+//  * trunc(RN(q + 0.5*sign q)) = sign(q) * floor(RN(|q| + 0.5)) (RN is
+//    symmetric): u = RN(|q| + 0.5) as the reference's addition rounds it, and
+//    for 0 <= u < 2^23 the low byte of the bits of RD(u + 2^23) is floor(u)
+//    (the ulp there is 1), so no conversion is needed.  |q| < 127.5 here, so
+//    floor(u) <= 127; the sign is applied as (i ^ s) - s with s = 0 or -1.
 __device__ __forceinline__ int8_t sage_i8(float x, float scale, float rscale) {
   const float q0 = __fmul_rn(x, rscale);
   const float r = __fmaf_rn(-q0, scale, x);
   const float q = __fmaf_rn(r, rscale, q0);
-  const float big = __fadd_rn(q, 12582912.f);
-  const float rne = __fsub_rn(big, 12582912.f);
-  const float d = __fsub_rn(q, rne);
-  int i = static_cast<int>(__float_as_uint(big) - 0x4B400000u);
-  if (d == 0.5f && q > 0.f) ++i;
-  if (d == -0.5f && q < 0.f) --i;
-  return static_cast<int8_t>(i);
+  const float u = __fadd_rn(fabsf(q), 0.5f);
+  const int mag = static_cast<int>(__float_as_uint(__fadd_rd(u, 8388608.f)) & 0xFFu);
+  const int s = static_cast<int>(__float_as_uint(q)) >> 31;
+  return static_cast<int8_t>((mag ^ s) - s);
 }
 
 template <int N>
