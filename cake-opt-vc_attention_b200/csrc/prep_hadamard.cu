@@ -165,6 +165,16 @@ __global__ void __launch_bounds__(kHadWarps * 32) had_tiles(HadParams p) {
     scale = __fdiv_rn(__uint_as_float(*amax), 448.f);
     if (scale == 0.f) scale = 1.f;
   }
+  // x / scale correctly rounded by Markstein's correction step (Handbook of
+  // Floating-Point Arithmetic, Muller et al., 2nd ed., sec. 4.7): with
+  // y = RN(1/scale), q0 = RN(x*y) and the exact remainder r = fma(-q0, scale, x),
+  // RN(q0 + r*y) = RN(x/scale) for normal quotients; a subnormal quotient
+  // encodes to a signed E4M3 zero either way.
+  const float rscale = __frcp_rn(scale);
+  auto div_scale = [&](float x) {
+    const float q0 = __fmul_rn(x, rscale);
+    return __fmaf_rn(__fmaf_rn(-q0, scale, x), rscale, q0);
+  };
   float mx = 0.f;
   for (int r = warp; r < rows; r += kHadWarps) {
     int64_t src = r0 + r;
@@ -185,7 +195,7 @@ __global__ void __launch_bounds__(kHadWarps * 32) had_tiles(HadParams p) {
       uint32_t packed[E / 2];
 #pragma unroll
       for (int i = 0; i < E / 2; ++i)
-        packed[i] = e4m3x2(__fdiv_rn(x[2 * i], scale), __fdiv_rn(x[2 * i + 1], scale));
+        packed[i] = e4m3x2(div_scale(x[2 * i]), div_scale(x[2 * i + 1]));
       uint8_t* dst = (isq ? p.q8 : p.k8) + ((bh * S) + r0 + r) * D + lane * E;
       if constexpr (E == 4) *reinterpret_cast<uint32_t*>(dst) = packed[0] | (packed[1] << 16);
       else *reinterpret_cast<uint16_t*>(dst) = static_cast<uint16_t>(packed[0]);
