@@ -106,6 +106,28 @@ __device__ __forceinline__ int8_t sage_i8(float x, float scale, float rscale) {
   return static_cast<int8_t>((mag ^ s) - s);
 }
 
+// Two values rounded to T (RN) and held packed; unpack is exact.
+template <typename T>
+struct Pair;
+template <>
+struct Pair<float> {
+  using type = float2;
+  static __device__ __forceinline__ float2 pack(float a, float b) { return make_float2(a, b); }
+  static __device__ __forceinline__ float2 unpack(float2 v) { return v; }
+};
+template <>
+struct Pair<__half> {
+  using type = __half2;
+  static __device__ __forceinline__ __half2 pack(float a, float b) { return __floats2half2_rn(a, b); }
+  static __device__ __forceinline__ float2 unpack(__half2 v) { return __half22float2(v); }
+};
+template <>
+struct Pair<__nv_bfloat16> {
+  using type = __nv_bfloat162;
+  static __device__ __forceinline__ __nv_bfloat162 pack(float a, float b) { return __floats2bfloat162_rn(a, b); }
+  static __device__ __forceinline__ float2 unpack(__nv_bfloat162 v) { return __bfloat1622float2(v); }
+};
+
 template <int N>
 __device__ __forceinline__ void store_i8(int8_t* p, const int8_t (&v)[N]) {
   if constexpr (N == 8) {
@@ -281,7 +303,10 @@ __global__ void __launch_bounds__(kTileThreads, 1) qk_tiles(QKTileParams p) {
 #pragma unroll
         for (int i = 0; i < E; ++i) kmv[i] = to_f32(kmp[i]);
       }
-      T x[8][E];   // centred values, exactly representable in T: keep them narrow
+      // centred values RN_T(k - km), exactly representable in T: kept narrow,
+      // and for 16-bit T rounded two at a time by the packed conversion
+      using P = Pair<T>;
+      typename P::type x[8][E / 2];
       float amax = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -290,14 +315,14 @@ __global__ void __launch_bounds__(kTileThreads, 1) qk_tiles(QKTileParams p) {
           float raw[E];
           load_vec_smem<T, E>(tile + r * D + col, raw);
 #pragma unroll
-          for (int j = 0; j < E; ++j) {
-            const float c = round_as(__fsub_rn(raw[j], kmv[j]), static_cast<T*>(nullptr));
-            x[i][j] = static_cast<T>(c);
-            amax = fmaxf(amax, fabsf(c));
+          for (int j = 0; j < E; j += 2) {
+            x[i][j / 2] = P::pack(__fsub_rn(raw[j], kmv[j]), __fsub_rn(raw[j + 1], kmv[j + 1]));
+            const float2 c = P::unpack(x[i][j / 2]);
+            amax = fmaxf(amax, fmaxf(fabsf(c.x), fabsf(c.y)));
           }
         } else {
 #pragma unroll
-          for (int j = 0; j < E; ++j) x[i][j] = static_cast<T>(0.f);
+          for (int j = 0; j < E; j += 2) x[i][j / 2] = P::pack(0.f, 0.f);
         }
       }
       amax = warp_max(amax);
@@ -315,7 +340,11 @@ __global__ void __launch_bounds__(kTileThreads, 1) qk_tiles(QKTileParams p) {
         const int r = 8 * (8 * ih + i) + 2 * tld + hf;
         int8_t o[E];
 #pragma unroll
-        for (int j = 0; j < E; ++j) o[j] = sage_i8(to_f32(x[i][j]), scale, rscale);
+        for (int j = 0; j < E; j += 2) {
+          const float2 c = P::unpack(x[i][j / 2]);
+          o[j] = sage_i8(c.x, scale, rscale);
+          o[j + 1] = sage_i8(c.y, scale, rscale);
+        }
         if (r < rows) store_i8<E>(p.k8 + (bh * S + r0 + r) * D + col, o);
       }
       if (lane == 0 && ih == 0) p.ks[bh * (p.ktiles * 4) + (r0 >> 7) * 4 + tld] = scale;
