@@ -190,6 +190,7 @@ __global__ void __launch_bounds__(kTileThreads) v_tile_quant(const T* __restrict
   uint8_t* sout = smem + G::kInBytes;
   float* s_mul = reinterpret_cast<float*>(smem + G::kInBytes + G::kOutBytes);  // recp or scale
   float* s_mean = s_mul + D;
+  float* s_rcp = s_mean + D;   // RN(1/s) for the residual modes' quotients
   const int64_t tile = blockIdx.x, bh = blockIdx.y;
   const int count = static_cast<int>(min64(128, S - tile * 128));
   stage_tile<T, D>(sin, v, bh, H, S, sb, sh, ss, perm, tile);
@@ -205,6 +206,7 @@ __global__ void __launch_bounds__(kTileThreads) v_tile_quant(const T* __restrict
       const float s = vs[bh * D + d];
       s_mul[d] = s;
       s_mean[d] = mean;
+      s_rcp[d] = __frcp_rn(s);
       means[(bh * tiles + tile) * D + d] = __float2half_rn(__fdiv_rn(mean, s));
     }
   }
@@ -218,6 +220,7 @@ __global__ void __launch_bounds__(kTileThreads) v_tile_quant(const T* __restrict
       s = fmaxf(s, __fdiv_rn(fabsf(mean), 65504.f));
       s_mul[d] = s;
       s_mean[d] = mean;
+      s_rcp[d] = __frcp_rn(s);
       vs[(bh * tiles + tile) * D + d] = s;
       means[(bh * tiles + tile) * D + d] = __float2half_rn(__fdiv_rn(mean, s));
     }
@@ -241,8 +244,14 @@ __global__ void __launch_bounds__(kTileThreads) v_tile_quant(const T* __restrict
         x0 = __fmul_rn(x0, s_mul[d]);
         x1 = __fmul_rn(x1, s_mul[d]);
       } else {
-        x0 = r0 < count ? __fdiv_rn(__fsub_rn(x0, s_mean[d]), s_mul[d]) : 0.f;
-        x1 = r0 + 1 < count ? __fdiv_rn(__fsub_rn(x1, s_mean[d]), s_mul[d]) : 0.f;
+        // (x - mean) / s correctly rounded by Markstein's correction step
+        // (Handbook of Floating-Point Arithmetic, sec. 4.7); a subnormal
+        // quotient encodes to a signed E4M3 zero either way
+        const float sd = s_mul[d], rd = s_rcp[d];
+        const float n0 = __fsub_rn(x0, s_mean[d]), n1 = __fsub_rn(x1, s_mean[d]);
+        const float a0 = __fmul_rn(n0, rd), a1 = __fmul_rn(n1, rd);
+        x0 = r0 < count ? __fmaf_rn(__fmaf_rn(-a0, sd, n0), rd, a0) : 0.f;
+        x1 = r0 + 1 < count ? __fmaf_rn(__fmaf_rn(-a1, sd, n1), rd, a1) : 0.f;
       }
       *reinterpret_cast<uint16_t*>(sout + d * 128 + r0) = e4m3x2(x0, x1);
     }
