@@ -87,6 +87,27 @@ def test_c_abi_rejects_bad_arguments_on_host(lib):
     assert lib.vc_kernel_resources(96, None) == N.VC_ERR_ARG
 
 
+def test_e4m3_qk_entries_reject_bad_arguments_on_host(lib):
+    """The Hadamard E4M3 Q/K prep and its attention entry validate on the
+    host before any device use."""
+    from vc_b200 import _native as N
+    p = C.c_void_p(1 << 20)                          # never dereferenced: rejected first
+    st = (2 * 300 * 128, 300 * 128, 128)
+    prep = lambda kqb, ws=1 << 24: lib.vc_prep_qk_hadamard_e4m3(
+        p, p, N.VC_DTYPE_BF16, 1, 2, 300, 300, 128, *st, *st, None, 1, None, None, kqb, p, p, p, p, p, ws, None)
+    assert prep(200) == N.VC_ERR_ARG and "k_quant_block" in _last(lib)
+    assert prep(8192) == N.VC_ERR_ARG and "k_quant_block" in _last(lib)
+    assert prep(256, ws=16) == N.VC_ERR_WORKSPACE and "workspace" in _last(lib)
+    assert lib.vc_prep_qk_hadamard_workspace_bytes(1, 2, 300, 300, 128, 100) < 0
+    assert lib.vc_prep_qk_hadamard_workspace_bytes(1, 2, 300, 300, 128, 256) > 0
+    args = [p] * 7 + [p, N.VC_DTYPE_BF16, 1, 2, 300, 300, 128, 2 * 300 * 128, 300 * 128, 128]
+    assert lib.vc_attention_fwd_e4m3qk(*args, 0, 0, 256, 0.125, 0, -1, None) == N.VC_ERR_UNSUPPORTED
+    assert "ExpCast" in _last(lib)
+    assert lib.vc_attention_fwd_e4m3qk(*args, 1, 0, 100, 0.125, 0, -1, None) == N.VC_ERR_ARG
+    assert lib.vc_attention_fwd_e4m3qk(*args, 1, 0, 256, -1.0, 0, -1, None) == N.VC_ERR_ARG
+    assert "sm_scale" in _last(lib)
+
+
 def test_status_codes_map_to_exceptions():
     from vc_b200 import _native as N
     N.check(N.VC_OK, "x")
