@@ -130,3 +130,52 @@ def test_full_size(ops, name):
     torch.cuda.synchronize()
     assert torch.equal(sharded, out)
     assert torch.equal(again, out)
+
+
+@pytest.mark.parametrize("name", ["c2", "c3"])
+def test_full_size_e4m3_qk(ops, name):
+    """The Config contract's own Q/K format (Hadamard rotation, E4M3 blocks of
+    128 Q rows and 256 K rows) at the full config shape, with the same checks:
+    whole-head payloads bit-exact, sampled rows within the tolerance of the
+    oracle on the same payloads, sharded and repeated calls bitwise equal."""
+    B, H, S, D, smooth, mixture, outliers = CONFIGS[name]
+    kqb = 256
+    q, k, v = _inputs(B, H, S, D, mixture, outliers)
+    perm = ops.group_values(v, 8, 2) if smooth else None
+    q8, qs, k8, ks, km = ops.prep_qk_hadamard(q, k, perm=perm, k_smooth=True, k_quant_block=kqb)
+    if smooth:
+        v8, vs, means = ops.prep_v_blocks(v, perm=perm, channel_scale=True)
+    else:
+        (v8, vs), means = ops.prep_v_channel(v), None
+    args = (q8, qs, k8, ks, v8, vs, means)
+    kw = dict(out_dtype=torch.float32, sm_scale=D ** -0.5, block_values=smooth, k_quant_block=kqb)
+    out = ops.attention_fwd(*args, **kw)
+    torch.cuda.synchronize()
+
+    rows = _rows(S)
+    for b, h in ((0, 0), (B - 1, H - 1)):
+        bs, hs = slice(b, b + 1), slice(h, h + 1)
+        ost = O.prepare_hadamard(q[bs, hs].cpu(), k[bs, hs].cpu(), k_smooth=True, k_quant_block=kqb,
+                                 km=km[bs, hs].cpu(), perm=perm[bs, hs].cpu() if smooth else None)
+        assert np.array_equal(_np(q8[bs, hs].view(torch.uint8)), ost["q"]), f"q8 {b},{h}"
+        assert np.array_equal(_np(qs[bs, hs]), ost["qs"]), f"qs {b},{h}"
+        assert np.array_equal(_np(k8[bs, hs].view(torch.uint8)), ost["k"]), f"k8 {b},{h}"
+        assert np.array_equal(_np(ks[bs, hs]), ost["ks"]), f"ks {b},{h}"
+        state = {**ost, "v": _np(v8[bs, hs].view(torch.uint8)), "vs": vs[bs, hs].cpu(),
+                 "means": _np(means[bs, hs]) if smooth else None, "expcast": True, "block_values": smooth,
+                 "scale": D ** -0.5}
+        ref = O.reference(state, query_indices=rows, chunk=128)
+        got = out[bs, hs].index_select(2, rows.cuda()).cpu()
+        m = O.metrics(got, ref)
+        print(f"{name} E4M3 QK head ({b},{h}): vs oracle {m}")
+        assert m["cos"] >= COS_MIN and m["rel_l2"] <= REL_MAX, (b, h, m)
+
+    units = B * H * ((S + 127) // 128)
+    cuts = (0, units // 3 + 7, 2 * units // 3 + 11, units)
+    sharded = torch.zeros_like(out)
+    for lo, hi in zip(cuts[:-1], cuts[1:]):
+        ops.attention_fwd(*args, out=sharded, unit_range=(lo, hi), **kw)
+    again = ops.attention_fwd(*args, **kw)
+    torch.cuda.synchronize()
+    assert torch.equal(sharded, out)
+    assert torch.equal(again, out)
