@@ -58,6 +58,7 @@ struct Params {
   int64_t nqs, nks, ktiles, qtiles;
   int64_t kq_tiles;   // E4M3 block Q/K: K tiles per K scale
   int64_t unit_begin, unit_end;   // units (b*H+h)*qtiles + q_tile to compute
+  int64_t pair_begin, qpairs;     // paired-tile kernel: first pair (b*H+h)*qpairs + q_tile/2, pairs per head
   float sm_scale;
   int exact_expcast;   // 1: unfused RN(RN(raw*f)-m) encoder instead of the folded affine one
 };
@@ -439,6 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 #include "attention_softmax.cuh"
 #include "attention_alt.cuh"
+#include "attention_pair.cuh"
 
 // ---------------------------------------------------------------------------
 // Host side: tensor maps and dispatch.
@@ -482,17 +484,30 @@ int launch_attn(const AttnArgs& a, const CUtensorMap& mk, const CUtensorMap& mv,
   return cudaGetLastError() == cudaSuccess ? VC_OK : VC_ERR_LAUNCH;
 }
 
-// VC_B200_KERNEL=general selects the general kernel (register accumulation)
-// for ExpCast + channel-scaled V as well; the default there is the
-// alternating-tile kernel.
+// VC_B200_KERNEL selects another kernel for ExpCast + channel-scaled V:
+// "general" (register accumulation) or "alt" (one Q tile per CTA, the two
+// softmax groups alternating K tiles); the default is the paired-tile kernel.
 bool use_general_kernel() {
   const char* e = getenv("VC_B200_KERNEL");
   return e && strcmp(e, "general") == 0;
 }
+bool use_alt_kernel() {
+  const char* e = getenv("VC_B200_KERNEL");
+  return e && strcmp(e, "alt") == 0;
+}
 
 struct Maps {
-  CUtensorMap k, v;
+  CUtensorMap q, k, v;
 };
+
+template <int D, typename OutT, bool BV, bool QF8 = false>
+int launch_pair(const Maps& m, const Params& p, int64_t pairs, cudaStream_t st) {
+  auto k = vc_attention_pair_kernel<D, OutT, BV, QF8>;
+  const int smem = PairSmem<D>::kAlloc;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return VC_ERR_LAUNCH;
+  k<<<static_cast<unsigned>(pairs), kPairThreads, smem, st>>>(m.q, m.k, m.v, p);
+  return cudaGetLastError() == cudaSuccess ? VC_OK : VC_ERR_LAUNCH;
+}
 
 template <int D, typename OutT, bool BV, bool QF8 = false>
 int launch_alt(const Maps& m, const Params& p, int64_t units, cudaStream_t st) {
@@ -504,12 +519,22 @@ int launch_alt(const Maps& m, const Params& p, int64_t units, cudaStream_t st) {
 }
 
 template <int D, typename OutT>
-int dispatch_flags(const AttnArgs& a, const Maps& m, const Params& p, int64_t units, cudaStream_t st) {
-  if (a.qk_e4m3) {   // E4M3 block Q/K: the alternating-tile kernel only (ExpCast, channel V scales)
-    if (a.block_values) return launch_alt<D, OutT, true, true>(m, p, units, st);
-    return launch_alt<D, OutT, false, true>(m, p, units, st);
+int dispatch_flags(const AttnArgs& a, const Maps& m, const Params& p, int64_t units, int64_t pairs,
+                   cudaStream_t st) {
+  const bool alt = use_alt_kernel();
+  if (a.qk_e4m3) {   // E4M3 block Q/K: the tensor-memory kernels only (ExpCast, channel V scales)
+    if (alt) {
+      if (a.block_values) return launch_alt<D, OutT, true, true>(m, p, units, st);
+      return launch_alt<D, OutT, false, true>(m, p, units, st);
+    }
+    if (a.block_values) return launch_pair<D, OutT, true, true>(m, p, pairs, st);
+    return launch_pair<D, OutT, false, true>(m, p, pairs, st);
   }
-  if (a.expcast && !a.vs_per_block && !use_general_kernel()) {
+  if (a.expcast && !a.vs_per_block && !use_general_kernel() && !alt) {
+    if (a.block_values) return launch_pair<D, OutT, true>(m, p, pairs, st);
+    return launch_pair<D, OutT, false>(m, p, pairs, st);
+  }
+  if (a.expcast && !a.vs_per_block && alt) {
     if (a.block_values) return launch_alt<D, OutT, true>(m, p, units, st);
     return launch_alt<D, OutT, false>(m, p, units, st);
   }
@@ -540,7 +565,7 @@ int attention_fwd(const AttnArgs& a, cudaStream_t st) {
   if (ue == ub) return VC_OK;
   Maps m;
   const CUtensorMapSwizzle swk = a.D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  if (!make_map_3d(&m.k, a.k8, a.D, a.Sk, BH, a.D, 128, swk) ||
+  if (!make_map_3d(&m.q, a.q8, a.D, a.Sq, BH, a.D, 128, swk) || !make_map_3d(&m.k, a.k8, a.D, a.Sk, BH, a.D, 128, swk) ||
       !make_map_3d(&m.v, a.v8, ktiles * 128, a.D, BH, 128, a.D, CU_TENSOR_MAP_SWIZZLE_128B)) {
     set_last_error("vc_attention_fwd: cuTensorMapEncodeTiled failed");
     return VC_ERR_LAUNCH;
@@ -565,15 +590,22 @@ int attention_fwd(const AttnArgs& a, cudaStream_t st) {
   p.qtiles = qtiles;
   p.unit_begin = ub;
   p.unit_end = ue;
+  // paired-tile kernel: the pairs (two consecutive Q tiles of one head) that meet [ub, ue)
+  p.qpairs = (qtiles + 1) / 2;
+  const int64_t pb = (ub / qtiles) * p.qpairs + (ub % qtiles) / 2;
+  const int64_t pe = ((ue - 1) / qtiles) * p.qpairs + ((ue - 1) % qtiles) / 2 + 1;
+  p.pair_begin = pb;
   p.sm_scale = a.sm_scale;
   p.exact_expcast = a.expcast == 2 ? 1 : 0;
-  const int64_t units = ue - ub;
+  const int64_t units = ue - ub, pairs = pe - pb;
   if (a.out_dtype == VC_DTYPE_BF16)
-    return a.D == 128 ? dispatch_flags<128, __nv_bfloat16>(a, m, p, units, st)
-                      : dispatch_flags<64, __nv_bfloat16>(a, m, p, units, st);
+    return a.D == 128 ? dispatch_flags<128, __nv_bfloat16>(a, m, p, units, pairs, st)
+                      : dispatch_flags<64, __nv_bfloat16>(a, m, p, units, pairs, st);
   if (a.out_dtype == VC_DTYPE_F32)
-    return a.D == 128 ? dispatch_flags<128, float>(a, m, p, units, st) : dispatch_flags<64, float>(a, m, p, units, st);
-  return a.D == 128 ? dispatch_flags<128, __half>(a, m, p, units, st) : dispatch_flags<64, __half>(a, m, p, units, st);
+    return a.D == 128 ? dispatch_flags<128, float>(a, m, p, units, pairs, st)
+                      : dispatch_flags<64, float>(a, m, p, units, pairs, st);
+  return a.D == 128 ? dispatch_flags<128, __half>(a, m, p, units, pairs, st)
+                    : dispatch_flags<64, __half>(a, m, p, units, pairs, st);
 }
 
 cudaError_t attention_error_word(uint32_t* code, bool clear) { return read_tu_error_word(code, clear); }

@@ -641,3 +641,58 @@ def test_hadamard_attention_cross_lengths_and_shards(ops):
     for r in ((0, 2), (2, 5), (5, units)):
         ops.attention_fwd(q8, qs, k8, ks, v8, vs, None, out=out, sm_scale=scale, unit_range=r)
     assert torch.equal(out, full)
+
+
+# Q-tile counts 1 (tile B of the only pair is empty), 2, 3 (last pair half
+# empty), 8; Sq != Sk; D 64 and 128; with and without block means
+PAIR_CASES = [
+    ((1, 2, 1000, 128), 1000, False),
+    ((2, 1, 385, 64), 385, False),
+    ((1, 1, 100, 128), 100, False),
+    ((1, 2, 256, 128), 700, False),
+    ((1, 1, 300, 64), 1300, True),
+    ((1, 2, 1000, 128), 1000, True),
+    ((2, 1, 129, 128), 2100, True),
+]
+
+
+@pytest.mark.parametrize("shape,sk,smooth", PAIR_CASES)
+def test_paired_tile_kernel_equals_alternating_kernel(ops, monkeypatch, shape, sk, smooth):
+    """The paired-tile kernel (two Q tiles per CTA, one softmax chain each)
+    performs every row's arithmetic in the same order as the alternating-tile
+    kernel (one Q tile per CTA, the groups alternating K tiles), so the two
+    give identical bits: INT8 and E4M3 Q/K, with and without block means, and
+    as unit ranges that cut pairs in two."""
+    B, H, Sq, D = shape
+    g = torch.Generator().manual_seed(51)
+    q = torch.randn(B, H, Sq, D, generator=g).to(torch.bfloat16)
+    k = (torch.randn(B, H, sk, D, generator=g) + 1.5 * torch.randn(B, H, 1, D, generator=g)).to(torch.bfloat16)
+    if smooth:
+        v = mixture_values(51, (B, H, sk, D), torch.bfloat16)
+    else:
+        v = torch.randn(B, H, sk, D, generator=g).to(torch.bfloat16)
+    qc, kc, vc = q.cuda(), k.cuda(), v.cuda()
+    perm = ops.group_values(vc, 8, 2) if smooth else None
+    if smooth:
+        v8, vs, means = ops.prep_v_blocks(vc, perm=perm, channel_scale=True)
+    else:
+        v8, vs = ops.prep_v_channel(vc)
+        means = None
+    payloads = [ops.prep_qk_int8(qc, kc, perm=perm)[:4],
+                ops.prep_qk_hadamard(qc, kc, perm=perm, k_smooth=True, k_quant_block=256)[:4]]
+    qtiles = (Sq + 127) // 128
+    for (q8, qs, k8, ks), scale in ((payloads[0], None), (payloads[0], 1.0), (payloads[1], None)):
+        kw = dict(out_dtype=torch.float32, block_values=smooth)
+        if scale is not None:
+            kw["sm_scale"] = scale
+        pair = ops.attention_fwd(q8, qs, k8, ks, v8, vs, means, **kw)
+        split = torch.full_like(pair, float("nan"))
+        cuts = sorted({0, min(1, B * H * qtiles), B * H * qtiles // 2 + 1, B * H * qtiles})
+        for b, e in zip(cuts[:-1], cuts[1:]):
+            ops.attention_fwd(q8, qs, k8, ks, v8, vs, means, out=split, unit_range=(b, e), **kw)
+        monkeypatch.setenv("VC_B200_KERNEL", "alt")
+        alt = ops.attention_fwd(q8, qs, k8, ks, v8, vs, means, **kw)
+        monkeypatch.delenv("VC_B200_KERNEL")
+        assert torch.equal(pair, alt)
+        assert torch.equal(split, pair)
+    assert ops.error_word(0, clear=True) == 0
