@@ -11,8 +11,9 @@ preparation and the fused attention kernel, inputs resident in HBM (the
   e2e    = same metric through the public API with pinned host buffers:
            H2D of the inputs + the call + D2H of the output every step
   roofline: the fused attention kernel, CUDA-event timed inside the region
-  cpu_baseline: the CPU oracle (a restatement of the reference's own CPU
-           path) on a bounded sample, extrapolated linearly
+  cpu_baseline: the reference's own CPU path (its Config API reference
+           backend, installed unmodified under baseline/_ref; else the CPU
+           oracle of this path) on a bounded sample, extrapolated linearly
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c2]
 Multi-GPU: torchrun --nproc-per-node N bench.py --gpus N (units split across
@@ -174,15 +175,63 @@ class ClockSampler:
                 "samples": len(sm), "scope": scope}
 
 
+REF_ROOT = REPO / "baseline" / "_ref"
+
+
+def _reference_core():
+    """The reference package installed unmodified under baseline/_ref (pure
+    Python, VC_ATTENTION_BUILD_CUDA=0), or None when it is absent."""
+    if not (REF_ROOT / "vc_attention" / "core.py").exists():
+        return None
+    if str(REF_ROOT) not in sys.path:
+        sys.path.insert(0, str(REF_ROOT))
+    from vc_attention import core
+    if not str(Path(core.__file__).resolve()).startswith(str(REF_ROOT.resolve())):
+        return None          # another vc_attention shadows the reference install
+    return core
+
+
 def cpu_baseline_sample(B, H, S, D, dtype, k_std, smooth, threads=None, gen=None):
-    """Time the CPU oracle on one head's preparation plus 128 query rows
-    against all keys; extrapolate linearly to the full workload."""
-    from oracle import vc_oracle as O
+    """Time the reference's CPU path on a bounded sample and extrapolate
+    linearly to the full workload.
+
+    With the reference installed under baseline/_ref ("reference"): its own
+    public API, ``vc_attention.core.attention(q, k, v, Config(backend=
+    "reference", expcast=True, v_smooth=...))`` (E4M3 encode/decode with FP32
+    matmul emulation, the numerical contract the north star names), on head 0
+    with 128 and 1024 sampled query rows against all keys (after one untimed
+    warm-up call); the two sizes give the per-call fixed cost (K/V
+    preparation) and the per-row cost.
+    Otherwise ("port"): the CPU oracle of this path (one head's INT8/FP8
+    preparation plus 128 query rows through the decoded-payload reference)."""
     if threads:
         torch.set_num_threads(threads)
     gen = gen or {}
     q, k, v = gen_head(0, S, D, dtype, k_std, gen.get("v_mixture", False), "cpu", outliers=gen.get("outliers", 0.0))
     q, k, v = (x.reshape(1, 1, S, D) for x in (q, k, v))
+    ops_full = 4.0 * B * H * S * S * D
+    core = _reference_core()
+    if core is not None:
+        cfg = core.Config(backend="reference", expcast=True, v_smooth=smooth)
+        qf, kf, vf = q.float(), k.float(), v.float()
+        times = {}
+        core.attention(qf[:, :, :16], kf, vf, cfg)      # warm-up: thread pool, allocator
+        for n in (128, 1024):
+            rows = torch.linspace(0, S - 1, n).round().long()
+            t0 = time.perf_counter()
+            core.attention(qf[:, :, rows], kf, vf, cfg)
+            times[n] = time.perf_counter() - t0
+        per_row = max((times[1024] - times[128]) / 896.0, 1e-12)
+        fixed = max(times[128] - 128 * per_row, 0.0)
+        t_full = B * H * (fixed + per_row * S)
+        return {"value": ops_full / t_full / 1e12, "unit": "TOPS", "cores": torch.get_num_threads(),
+                "kind": "reference", "extrapolated": True,
+                "sample": f"reference vc_attention.core.attention (baseline/_ref, unmodified) with "
+                          f"Config(backend='reference', expcast=True, v_smooth={smooth}) on head 0: 128 rows x {S} keys "
+                          f"{times[128]:.2f}s, 1024 rows {times[1024]:.2f}s -> fixed {fixed:.2f}s + {per_row*1e3:.2f} ms/row, "
+                          f"extrapolated linearly to {B*H} heads x {S} rows",
+                "seconds_extrapolated": t_full}
+    from oracle import vc_oracle as O
     t0 = time.perf_counter()
     st = O.prepare(q, k, v, expcast=True, v_smooth=smooth, km=O.k_mean(k))
     t_prep = time.perf_counter() - t0
@@ -191,15 +240,23 @@ def cpu_baseline_sample(B, H, S, D, dtype, k_std, smooth, threads=None, gen=None
     O.reference(st, query_indices=rows, chunk=128)
     t_ref = time.perf_counter() - t0
     t_full = B * H * (t_prep + t_ref * (S / rows.numel()))
-    ops_full = 4.0 * B * H * S * S * D
     return {"value": ops_full / t_full / 1e12, "unit": "TOPS", "cores": torch.get_num_threads(), "kind": "port",
+            "extrapolated": True,
             "sample": f"CPU oracle: head-0 prep ({t_prep:.2f}s) + {rows.numel()} query rows x {S} keys "
                       f"({t_ref:.2f}s), extrapolated linearly to {B*H} heads x {S} rows",
             "seconds_extrapolated": t_full}
 
 
+def config_dict(desc, B, H, S, D, smooth, world):
+    """The ``config`` object both arms print (same keys and values)."""
+    return {"workload": desc, "B": B, "H": H, "S": S, "D": D, "expcast": True, "v_smooth": smooth,
+            "parallelism": f"units split over {world} rank(s), outputs sharded",
+            "l2": "inputs (811 MB) exceed the 126 MB L2; no flush needed"}
+
+
 def run_reference(args, cfg):
-    """--impl reference: the CPU oracle of the reference's path on host cores."""
+    """--impl reference: the reference's own CPU path on the host cores
+    (rank 0 only; other ranks exit without work)."""
     B, H, S, D, dtype, k_std, smooth, desc = cfg
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -215,8 +272,11 @@ def run_reference(args, cfg):
     ms = 4.0 * B * H * S * S * D / (value * 1e12) * 1e3
     line = {"metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int8/e4m3 (decoded FP32 CPU emulation)", "data": "synthetic",
-            "config": {"workload": desc, "impl": "reference"}, "impl": "reference",
+            "vs_baseline": None, "dtype": "fp32 (E4M3 encode/decode emulation on the CPU)", "data": "synthetic",
+            "config": config_dict(desc, B, H, S, D, smooth, args.gpus), "impl": "reference",
+            "extrapolated": True,
+            "note": "each step times a bounded sample of the workload on the host cores; ms_per_step and value "
+                    "are that sample extrapolated linearly to the full call (see cpu_baseline.sample)",
             "cpu_baseline": {**vals[-1], "value": value},
             "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
@@ -418,9 +478,7 @@ def main():
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "int8 QK / e4m3 PV (fp32 accumulate), bf16 I/O",
                 "data": "synthetic (seeded per head on device)",
-                "config": {"workload": desc, "B": B, "H": H, "S": S, "D": D, "expcast": True, "v_smooth": smooth,
-                           "parallelism": f"units split over {world} rank(s), outputs sharded",
-                           "l2": "inputs (811 MB) exceed the 126 MB L2; no flush needed"},
+                "config": config_dict(desc, B, H, S, D, smooth, world),
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
                 "gpu_launches": launches_per_step * args.steps, "attention_ms": att_ms}
         if gather_ms is not None:

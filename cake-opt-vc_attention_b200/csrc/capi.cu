@@ -150,12 +150,13 @@ int vc_error_read(int device, uint32_t* code, int clear) {
     set_last_error("vc_error_read: bad device %d", device);
     return VC_ERR_ARG;
   }
-  uint32_t words[4] = {0, 0, 0, 0};
+  uint32_t words[5] = {0, 0, 0, 0, 0};
   cudaError_t e = attention_error_word(&words[0], clear != 0);
   if (e == cudaSuccess) e = prep_qk_error_word(&words[1], clear != 0);
   if (e == cudaSuccess) e = prep_v_error_word(&words[2], clear != 0);
   if (e == cudaSuccess) e = prep_hadamard_error_word(&words[3], clear != 0);
-  *code = words[0] | words[1] | words[2] | words[3];
+  if (e == cudaSuccess) e = tensor_peak_error_word(&words[4], clear != 0);
+  *code = words[0] | words[1] | words[2] | words[3] | words[4];
   cudaSetDevice(prev);
   if (e != cudaSuccess) {
     set_last_error("vc_error_read: %s", cudaGetErrorString(e));
@@ -409,6 +410,18 @@ int vc_attention_fwd_e4m3qk(const uint8_t* q8, const float* qs, const uint8_t* k
              out_dtype, B, H, Sq, Sk, D, out_stride_b, out_stride_h, out_stride_s, expcast, block_values ? 1 : 0, 0,
              sm_scale, unit_begin, unit_end, 1, k_quant_block};
   return finish(fn, attention_fwd(a, static_cast<cudaStream_t>(stream)));
+}
+
+int vc_tensor_peak(int kind, int n, int64_t iters, int ctas, int a_tmem, int nacc, unsigned long long* stamps,
+                   void* stream) {
+  const int64_t stride = (n + 31) / 32 * 32;
+  if ((kind != 0 && kind != 1) || n < 16 || n > 256 || n % 16 || nacc < 1 || nacc * stride > (a_tmem ? 448 : 512) || iters < 1 || iters > (int64_t(1) << 22) ||
+      ctas < 1 || ctas > 4096) {
+    set_last_error("vc_tensor_peak: kind 0/1, n a multiple of 16 in [16, 256], nacc accumulators of ceil(n/32)*32 columns within 512 (448 with A in tensor memory), iters in [1, 2^22], ctas in [1, 4096]");
+    return VC_ERR_ARG;
+  }
+  if (int rc = check_device()) return rc;
+  return finish("vc_tensor_peak", tensor_peak(kind, n, iters, ctas, a_tmem ? 1 : 0, nacc, stamps, static_cast<cudaStream_t>(stream)));
 }
 
 int vc_kernel_resources(int head_dim, int64_t* out4) {

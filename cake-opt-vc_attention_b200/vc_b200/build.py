@@ -23,7 +23,7 @@ CSRC = ROOT / "csrc"
 INCLUDE = REPO / "include"
 LIB = PKG / "libvc_b200.so"
 OBJ_DIR = ROOT / "_build"
-SOURCES = ["capi.cu", "prep_qk.cu", "prep_hadamard.cu", "prep_v.cu", "cluster.cu", "attention.cu"]
+SOURCES = ["capi.cu", "prep_qk.cu", "prep_hadamard.cu", "prep_v.cu", "cluster.cu", "attention.cu", "tensor_peak.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # Whole-program device code (no -rdc): ptxas honours setmaxnreg only then.
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3", "--expt-relaxed-constexpr",

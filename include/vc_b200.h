@@ -195,6 +195,21 @@ int vc_attention_fwd_e4m3qk(const uint8_t* q8, const float* qs, const uint8_t* k
  * Replaces _vc_sm90.kernel_resources (csrc/vc/vc_sm90.cu:788-822). */
 int vc_kernel_resources(int head_dim, int64_t* out4);
 
+/* Tensor-core throughput probe, the measured denominator of the attention
+ * kernel's roofline (a measurement aid; the reference quotes a nominal peak
+ * instead, scripts/profile_int8_h200.py).  Launches ``ctas`` CTAs (one per
+ * SM) that each issue iters x 4 MMAs of M=128, N=n, K=32 from shared-memory
+ * operands: kind 0 = tcgen05 kind::i8 (s32 accumulate), kind 1 = kind::f8f6f4
+ * with E4M3 operands (f32 accumulate); ``a_tmem`` != 0 reads A from tensor
+ * memory instead of shared memory; the MMAs accumulate into ``nacc``
+ * accumulators in turn (nacc * ceil(n/32)*32 columns must fit in 512, or in
+ * 448 with A in tensor memory).  ``stamps`` (optional, device, 3 per
+ * CTA) receives the issue and completion cycles and an ok flag.  The caller
+ * times the launch (ops = 2*128*n*32*4*iters*ctas).  n in [16,256] step 16,
+ * iters in [1, 2^22]. */
+int vc_tensor_peak(int kind, int n, int64_t iters, int ctas, int a_tmem, int nacc, unsigned long long* stamps,
+                   void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,7 +1,7 @@
 """Generate golden fixtures from the reference's own Python code.
 
-Run in a container that has the reference checkout (default path given by
-``--reference``).  It imports, by path:
+Run in a container that has the reference checkout (its path given by
+``--reference`` or the VC_REFERENCE_ROOT environment variable).  It imports, by path:
   * third_party/sageattention_local/sageattention_local/vc_reference.py
     (the reference's decoded-payload FP32 oracle),
   * third_party/sageattention_local/sageattention_local/triton/quant_per_thread.py
@@ -49,10 +49,13 @@ def sage_state(st):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("VC_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("VC_REFERENCE_ROOT"),
+                    help="path of the reference checkout (or set VC_REFERENCE_ROOT)")
     ap.add_argument("--hadamard", action="store_true",
                     help="only (re)write the Hadamard / E4M3 block-QK fixtures (step 5)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference <path-to-reference> or set VC_REFERENCE_ROOT")
     ref = Path(args.reference)
     if args.hadamard:
         sys.path.insert(0, str(ref / "src"))
