@@ -244,9 +244,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           mbar_arrive(&bar->mean_full[kb & 1]);
         }
       }
-    } else if (warp == 9 && lane == 0) {
+    } else if (warp == 9) {
       // ------------------------------------------------------- QK^T issuer
-      // issue n = 2j + X into slot n % NS once the scores of issue n - NS are read
+      // issue n = 2j + X into slot n % NS once the scores of issue n - NS are
+      // read.  The loop runs in the whole warp (descriptor arithmetic stays
+      // warp-uniform) and one elected lane issues each MMA and commit.
       constexpr uint32_t idesc_qk = QF8 ? idesc_make(1, 0, 0, 128, 128) : idesc_make(2, 1, 1, 128, 128);
       constexpr uint32_t idesc_preset = idesc_make(1, 0, 0, 128, 128);   // f32 <- f16 x f16
       const uint64_t adesc_preset = smem_desc_plain(smem_u32(smem + L::kOffPresetA), 128, 256);
@@ -254,36 +256,41 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       const uint64_t kdesc0 = kmajor_desc<D>(smem_u32(smem + L::kOffK));
       const uint64_t qdesc0 = kmajor_desc<D>(smem_u32(smem + L::kOffQ));
       constexpr uint64_t kStep = (L::kK >> 4);   // descriptor start-address units per K stage / Q tile
-      bool ok = mbar_wait(&bar->q_full, 0, kErrTimeoutMma);
+      bool ok = mbar_wait_warp(&bar->q_full, 0, kErrTimeoutMma);
       for (int j = 0; j < T && ok; ++j) {
         const int s = j % kPKS;
-        if (!mbar_wait(&bar->k_full[s], (j / kPKS) & 1, kErrTimeoutMma)) break;
+        if (!mbar_wait_warp(&bar->k_full[s], (j / kPKS) & 1, kErrTimeoutMma)) break;
         const uint64_t kd = kdesc0 + s * kStep;
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
           const int n = 2 * j + x, prev = n - C::kNS;
-          if (prev >= 0 && !mbar_wait(&bar->s_free[prev & 1], (prev >> 1) & 1, kErrTimeoutMma)) {
+          if (prev >= 0 && !mbar_wait_warp(&bar->s_free[prev & 1], (prev >> 1) & 1, kErrTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t scol = tmem + C::kS + 128 * (n % C::kNS);
           const uint64_t qd = qdesc0 + x * kStep;
-          if constexpr (QF8) {
+          if (elect_one()) {
+            if constexpr (QF8) {
 #pragma unroll
-            for (int kk = 0; kk < D / 32; ++kk) mma_f8_ss(scol, qd + 2 * kk, kd + 2 * kk, idesc_qk, kk > 0 ? 1u : 0u);
-          } else {
-            mma_f16_ss(scol, adesc_preset, bdesc_preset, idesc_preset, 0u);   // S = the bits of 1.5*2^23
+              for (int kk = 0; kk < D / 32; ++kk) mma_f8_ss(scol, qd + 2 * kk, kd + 2 * kk, idesc_qk, kk > 0 ? 1u : 0u);
+            } else {
+              mma_f16_ss(scol, adesc_preset, bdesc_preset, idesc_preset, 0u);   // S = the bits of 1.5*2^23
 #pragma unroll
-            for (int kk = 0; kk < D / 32; ++kk) mma_i8_ss(scol, qd + 2 * kk, kd + 2 * kk, idesc_qk, 1u);
+              for (int kk = 0; kk < D / 32; ++kk) mma_i8_ss(scol, qd + 2 * kk, kd + 2 * kk, idesc_qk, 1u);
+            }
+            mma_commit(&bar->s_full[x]);
           }
-          mma_commit(&bar->s_full[x]);
+          __syncwarp();
         }
         if (!ok) break;
-        mma_commit(&bar->k_empty[s]);
+        if (elect_one()) mma_commit(&bar->k_empty[s]);
+        __syncwarp();
       }
-    } else if (warp == 11 && lane == 0) {
+    } else if (warp == 11) {
       // ---------------------------------------------------------- P.V issuer
+      // (whole warp, one elected lane per MMA and commit, as above)
       constexpr uint32_t idesc_pv = idesc_make(1, 0, 0, 128, D + 16);  // f32 <- e4m3 x e4m3
       constexpr uint32_t idesc_mean = idesc_make(1, 0, 0, 128, D);     // f32 <- f16 x f16
       const uint64_t vdesc0 = smem_desc_sw128(smem_u32(smem + L::kOffV));
@@ -295,50 +302,60 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       bool ok = true;
       for (int j = 0; j < T && ok; ++j) {
         const int s = j % kPVS;
-        if (!mbar_wait(&bar->v_full[s], (j / kPVS) & 1, kErrTimeoutMma)) break;
+        if (!mbar_wait_warp(&bar->v_full[s], (j / kPVS) & 1, kErrTimeoutMma)) break;
         const uint64_t vd = vdesc0 + s * kStepV;
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
-          if (!mbar_wait(&bar->p_full[x], j & 1, kErrTimeoutMma)) {
+          if (!mbar_wait_warp(&bar->p_full[x], j & 1, kErrTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t ocol = tmem + (x ? C::kOB : C::kOA);
           const uint32_t pcol = tmem + (x ? C::kPB : C::kPA);
+          if (elect_one()) {
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_f8_ts(ocol, pcol + kk * 8, vd + 2 * kk, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < 4; ++kk)
+              mma_f8_ts(ocol, pcol + kk * 8, vd + 2 * kk, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          __syncwarp();
           if (BV && j >= 8 && (j & 7) == 0) {
             // batch kb of tile X, completed by its tile-j bookkeeping while PV_X(j) runs
             const int kb = (j >> 3) - 1;
-            if (!mbar_wait(&bar->a_full[x], kb & 1, kErrTimeoutMma) ||
-                !mbar_wait(&bar->mean_full[kb & 1], (kb >> 1) & 1, kErrTimeoutMma)) {
+            if (!mbar_wait_warp(&bar->a_full[x], kb & 1, kErrTimeoutMma) ||
+                !mbar_wait_warp(&bar->mean_full[kb & 1], (kb >> 1) & 1, kErrTimeoutMma)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            mma_f16_ss(ocol, massdesc0 + x * kStepMass, meandesc0 + (kb & 1) * kStepMean, idesc_mean, 1u);
+            if (elect_one())
+              mma_f16_ss(ocol, massdesc0 + x * kStepMass, meandesc0 + (kb & 1) * kStepMean, idesc_mean, 1u);
+            __syncwarp();
           }
-          mma_commit(&bar->pv_done[x]);
+          if (elect_one()) mma_commit(&bar->pv_done[x]);
+          __syncwarp();
         }
         if (!ok) break;
-        mma_commit(&bar->v_empty[s]);
+        if (elect_one()) mma_commit(&bar->v_empty[s]);
+        __syncwarp();
       }
 #pragma unroll
       for (int x = 0; x < 2; ++x) {
         if constexpr (BV) {
           // the open batch of tile X, written by its group after the loop
           const int kb = (T - 1) >> 3;
-          if (ok) ok = mbar_wait(&bar->a_full[x], kb & 1, kErrTimeoutMma) &&
-                       mbar_wait(&bar->mean_full[kb & 1], (kb >> 1) & 1, kErrTimeoutMma);
+          if (ok) ok = mbar_wait_warp(&bar->a_full[x], kb & 1, kErrTimeoutMma) &&
+                       mbar_wait_warp(&bar->mean_full[kb & 1], (kb >> 1) & 1, kErrTimeoutMma);
           if (ok) {
             tc_fence_after();
-            mma_f16_ss(tmem + (x ? C::kOB : C::kOA), massdesc0 + x * kStepMass, meandesc0 + (kb & 1) * kStepMean,
-                       idesc_mean, 1u);
+            if (elect_one())
+              mma_f16_ss(tmem + (x ? C::kOB : C::kOA), massdesc0 + x * kStepMass, meandesc0 + (kb & 1) * kStepMean,
+                         idesc_mean, 1u);
+            __syncwarp();
           }
         }
-        if (ok) mma_commit(&bar->o_final[x]);
+        if (ok && elect_one()) mma_commit(&bar->o_final[x]);
+        __syncwarp();
       }
     }
   } else {

@@ -23,6 +23,21 @@ __global__ void expcast_kernel(const float* __restrict__ x, uint8_t* __restrict_
   }
 }
 
+// Failure-detection self-test: warp 0 waits, through the same bounded wait
+// the kernels use, for an mbarrier phase that nothing completes.  The wait
+// gives up after ``budget_ns``, sets kErrTimeoutSelfTest in the error word
+// and the kernel returns normally.  ok_out[0] = 1 if the wait had succeeded.
+__global__ void wait_selftest_kernel(uint64_t budget_ns, int* ok_out) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);   // one arrival completes phase 0; none is made
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const bool ok = __all_sync(0xffffffffu, mbar_wait_budget(&bar, 0, kErrTimeoutSelfTest, budget_ns));
+  if (threadIdx.x == 0 && ok_out) ok_out[0] = ok ? 1 : 0;
+}
+
 // sm_100 check, cached per device.
 int check_device() {
   static std::mutex mu;
@@ -150,13 +165,14 @@ int vc_error_read(int device, uint32_t* code, int clear) {
     set_last_error("vc_error_read: bad device %d", device);
     return VC_ERR_ARG;
   }
-  uint32_t words[5] = {0, 0, 0, 0, 0};
+  uint32_t words[6] = {0, 0, 0, 0, 0, 0};
   cudaError_t e = attention_error_word(&words[0], clear != 0);
+  if (e == cudaSuccess) e = read_tu_error_word(&words[5], clear != 0);   // this file: the wait self-test
   if (e == cudaSuccess) e = prep_qk_error_word(&words[1], clear != 0);
   if (e == cudaSuccess) e = prep_v_error_word(&words[2], clear != 0);
   if (e == cudaSuccess) e = prep_hadamard_error_word(&words[3], clear != 0);
   if (e == cudaSuccess) e = tensor_peak_error_word(&words[4], clear != 0);
-  *code = words[0] | words[1] | words[2] | words[3] | words[4];
+  *code = words[0] | words[1] | words[2] | words[3] | words[4] | words[5];
   cudaSetDevice(prev);
   if (e != cudaSuccess) {
     set_last_error("vc_error_read: %s", cudaGetErrorString(e));
@@ -412,16 +428,26 @@ int vc_attention_fwd_e4m3qk(const uint8_t* q8, const float* qs, const uint8_t* k
   return finish(fn, attention_fwd(a, static_cast<cudaStream_t>(stream)));
 }
 
-int vc_tensor_peak(int kind, int n, int64_t iters, int ctas, int a_tmem, int nacc, unsigned long long* stamps,
+int vc_tensor_peak(int kind, int n, int64_t iters, int ctas, int a_tmem, int issuers, unsigned long long* stamps,
                    void* stream) {
   const int64_t stride = (n + 31) / 32 * 32;
-  if ((kind != 0 && kind != 1) || n < 16 || n > 256 || n % 16 || nacc < 1 || nacc * stride > (a_tmem ? 448 : 512) || iters < 1 || iters > (int64_t(1) << 22) ||
+  if ((kind != 0 && kind != 1) || n < 16 || n > 256 || n % 16 || issuers < 1 || issuers > 4 || issuers * stride > (a_tmem ? 448 : 512) || iters < 1 || iters > (int64_t(1) << 22) ||
       ctas < 1 || ctas > 4096) {
-    set_last_error("vc_tensor_peak: kind 0/1, n a multiple of 16 in [16, 256], nacc accumulators of ceil(n/32)*32 columns within 512 (448 with A in tensor memory), iters in [1, 2^22], ctas in [1, 4096]");
+    set_last_error("vc_tensor_peak: kind 0/1, n a multiple of 16 in [16, 256], 1-4 issuing warps whose accumulators of ceil(n/32)*32 columns fit in 512 (448 with A in tensor memory), iters in [1, 2^22], ctas in [1, 4096]");
     return VC_ERR_ARG;
   }
   if (int rc = check_device()) return rc;
-  return finish("vc_tensor_peak", tensor_peak(kind, n, iters, ctas, a_tmem ? 1 : 0, nacc, stamps, static_cast<cudaStream_t>(stream)));
+  return finish("vc_tensor_peak", tensor_peak(kind, n, iters, ctas, a_tmem ? 1 : 0, issuers, stamps, static_cast<cudaStream_t>(stream)));
+}
+
+int vc_selftest_wait_timeout(int64_t budget_ns, int* ok_out, void* stream) {
+  if (budget_ns < 1000 || budget_ns > 2000000000) {
+    set_last_error("vc_selftest_wait_timeout: budget_ns must be in [1e3, 2e9]");
+    return VC_ERR_ARG;
+  }
+  if (int rc = check_device()) return rc;
+  wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<uint64_t>(budget_ns), ok_out);
+  return finish("vc_selftest_wait_timeout", cudaGetLastError() == cudaSuccess ? VC_OK : VC_ERR_LAUNCH);
 }
 
 int vc_kernel_resources(int head_dim, int64_t* out4) {

@@ -12,13 +12,24 @@
 //   * stable order of tokens inside each cluster.
 // Unlike the reference (shared-memory atomics), the centre statistics here are
 // accumulated in a fixed order, so results are bitwise reproducible.
+//
+// More than 8 effective centres (up to 256) take the wide path, the policy of
+// the reference's public entry for that range (csrc/vc/pybind.cpp:6-44, its
+// legacy Lloyd loop): distances (|x|^2 + |c|^2) - 2 x.c in FP32 (the
+// reference uses a matmul; rounding order differs, ties still pick the lowest
+// centre), centre = member mean (empty centres keep their value), stable
+// argsort of the final labels.  Here: assignment kernel with the head's
+// centres in shared memory, one token per thread; then the stable counting
+// sort below; then each centre's mean summed over its members in sorted
+// token order (deterministic, no atomics).
 #include "common.cuh"
 #include "kernels.h"
 
 namespace vcb {
 namespace {
 
-constexpr int kMaxC = 8;
+constexpr int kMaxC = 8;        // fused path
+constexpr int kWideMaxC = 256;  // wide path (the reference's public maximum)
 constexpr int kRows = 128;
 constexpr int kChunk = 1024;  // tokens per sort chunk
 
@@ -234,9 +245,9 @@ __global__ void grp_update(float* __restrict__ centers, const float* __restrict_
 // Stable counting sort, step 1: label histogram per chunk of kChunk tokens.
 __global__ void grp_hist(const int32_t* __restrict__ labels, int64_t S, int count, int32_t* __restrict__ hist,
                          int64_t nchunk) {
-  __shared__ int h[kMaxC];
+  __shared__ int h[kWideMaxC];
   const int64_t bh = blockIdx.y, chunk = blockIdx.x;
-  if (threadIdx.x < kMaxC) h[threadIdx.x] = 0;
+  if (threadIdx.x < kWideMaxC) h[threadIdx.x] = 0;
   __syncthreads();
   for (int64_t i = chunk * kChunk + threadIdx.x; i < min64(S, (chunk + 1) * kChunk); i += blockDim.x)
     atomicAdd(&h[labels[bh * S + i]], 1);
@@ -269,10 +280,10 @@ __global__ void grp_scan(int32_t* __restrict__ hist, int count, int64_t nchunk) 
 // Step 3: one warp per chunk places tokens in order (ranks via match_any).
 __global__ void grp_scatter(const int32_t* __restrict__ labels, int64_t S, int count, const int32_t* __restrict__ offs,
                             int64_t nchunk, int64_t* __restrict__ perm) {
-  __shared__ int run[kMaxC];
+  __shared__ int run[kWideMaxC];
   const int64_t bh = blockIdx.y, chunk = blockIdx.x;
   const int lane = threadIdx.x;
-  if (lane < count) run[lane] = offs[(bh * nchunk + chunk) * count + lane];
+  for (int c = lane; c < count; c += 32) run[c] = offs[(bh * nchunk + chunk) * count + c];
   __syncwarp();
   const int64_t end = min64(S, (chunk + 1) * kChunk);
   for (int64_t base = chunk * kChunk; base < end; base += 32) {
@@ -286,6 +297,122 @@ __global__ void grp_scatter(const int32_t* __restrict__ labels, int64_t S, int c
     if (active && rank == 0) run[lb] += __popc(peers);
     __syncwarp();
   }
+}
+
+// Wide path, assignment: the head's ``count`` centres (FP32) and their
+// squared norms in shared memory; thread r owns token r of a 128-token tile
+// with the token's channels in registers.  dist = (|x|^2 + |c|^2) - 2 x.c,
+// the lowest index wins ties.
+template <typename T, int D>
+__global__ void __launch_bounds__(128) grp_assign_wide(const T* __restrict__ v, int64_t H, int64_t S, int64_t sb,
+                                                       int64_t sh, int64_t ss, int count,
+                                                       const float* __restrict__ centers, int32_t* __restrict__ labels) {
+  extern __shared__ __align__(16) float wide_sm[];
+  float* cen = wide_sm;                 // [count][D]
+  float* cnorm = wide_sm + count * D;   // [count]
+  const int64_t bh = blockIdx.y, tile = blockIdx.x;
+  const int64_t b = bh / H, h = bh - b * H;
+  const float4* src = reinterpret_cast<const float4*>(centers + bh * count * D);
+  for (int i = threadIdx.x; i < count * D / 4; i += 128) reinterpret_cast<float4*>(cen)[i] = src[i];
+  __syncthreads();
+  for (int c = threadIdx.x; c < count; c += 128) {
+    float n = 0.f;
+    for (int d = 0; d < D; ++d) n = __fadd_rn(n, __fmul_rn(cen[c * D + d], cen[c * D + d]));
+    cnorm[c] = n;
+  }
+  __syncthreads();
+  const int64_t row = tile * 128 + threadIdx.x;
+  if (row >= S) return;
+  float x[D];
+  load_vec<T, D>(v + b * sb + h * sh + row * ss, x);
+  float norm = 0.f;
+#pragma unroll
+  for (int d = 0; d < D; ++d) norm = __fadd_rn(norm, __fmul_rn(x[d], x[d]));
+  float best_d = __int_as_float(0x7f800000);
+  int best = 0;
+  for (int c = 0; c < count; ++c) {
+    const float4* cr = reinterpret_cast<const float4*>(cen + c * D);
+    float p[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int d4 = 0; d4 < D / 4; ++d4) {
+      const float4 cv = cr[d4];
+      p[0] = __fmaf_rn(x[4 * d4 + 0], cv.x, p[0]);
+      p[1] = __fmaf_rn(x[4 * d4 + 1], cv.y, p[1]);
+      p[2] = __fmaf_rn(x[4 * d4 + 2], cv.z, p[2]);
+      p[3] = __fmaf_rn(x[4 * d4 + 3], cv.w, p[3]);
+    }
+    const float dot = __fadd_rn(__fadd_rn(p[0], p[1]), __fadd_rn(p[2], p[3]));
+    const float dist = __fsub_rn(__fadd_rn(norm, cnorm[c]), __fmul_rn(2.f, dot));
+    if (dist < best_d) {
+      best_d = dist;
+      best = c;
+    }
+  }
+  labels[bh * S + row] = best;
+}
+
+// Wide path, update: centre c = the mean of its members, summed in sorted
+// (stable, token) order; members are perm[start_c .. start_c+1) from the
+// counting sort.  Thread d owns channel d; 16 member rows are loaded at once.
+template <typename T, int D>
+__global__ void grp_update_wide(const T* __restrict__ v, int64_t H, int64_t S, int64_t sb, int64_t sh, int64_t ss,
+                                int count, const int32_t* __restrict__ offs, int64_t nchunk,
+                                const int64_t* __restrict__ perm, float* __restrict__ centers) {
+  const int c = blockIdx.x;
+  const int64_t bh = blockIdx.y;
+  const int64_t b = bh / H, h = bh - b * H;
+  const int d = threadIdx.x;
+  const int64_t start = offs[(bh * nchunk) * count + c];
+  const int64_t end = c + 1 < count ? offs[(bh * nchunk) * count + c + 1] : S;
+  const T* vbh = v + b * sb + h * sh + d;
+  const int64_t* pr = perm + bh * S;
+  float s = 0.f;
+  int64_t i = start;
+  for (; i + 16 <= end; i += 16) {
+    float x[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) x[u] = to_f32(vbh[pr[i + u] * ss]);
+#pragma unroll
+    for (int u = 0; u < 16; ++u) s = __fadd_rn(s, x[u]);
+  }
+  for (; i < end; ++i) s = __fadd_rn(s, to_f32(vbh[pr[i] * ss]));
+  if (end > start) centers[(bh * count + c) * D + d] = __fdiv_rn(s, static_cast<float>(end - start));
+}
+
+template <typename T, int D>
+int launch_group_wide(const GroupArgs& a, cudaStream_t st) {
+  const int64_t BH = a.B * a.H, S = a.S;
+  const int count = static_cast<int>(min64(a.clusters, S));
+  const int64_t tiles = (S + 127) / 128, nchunk = (S + kChunk - 1) / kChunk;
+  char* w = static_cast<char*>(a.workspace);
+  float* centers = reinterpret_cast<float*>(w);
+  w += ((BH * count * D * 4 + 255) / 256) * 256;
+  int32_t* labels = reinterpret_cast<int32_t*>(w);
+  w += ((BH * S * 4 + 255) / 256) * 256;
+  int32_t* hist = reinterpret_cast<int32_t*>(w);
+  const T* v = static_cast<const T*>(a.v);
+  const int smem = count * D * 4 + count * 4;
+  if (cudaFuncSetAttribute(grp_assign_wide<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return VC_ERR_LAUNCH;
+  if (a.centers_in)
+    cudaMemcpyAsync(centers, a.centers_in, BH * count * D * 4, cudaMemcpyDeviceToDevice, st);
+  else
+    grp_init<T, D><<<BH, 128, 0, st>>>(v, a.H, S, a.sb, a.sh, a.ss, count, centers);
+  for (int it = 0; it < a.iterations; ++it) {
+    grp_assign_wide<T, D><<<dim3(tiles, BH), 128, smem, st>>>(v, a.H, S, a.sb, a.sh, a.ss, count, centers, labels);
+    // the stable sort of the labels: the permutation (final) or the members per centre (update)
+    grp_hist<<<dim3(nchunk, BH), 256, 0, st>>>(labels, S, count, hist, nchunk);
+    grp_scan<<<BH, 32, 0, st>>>(hist, count, nchunk);
+    grp_scatter<<<dim3(nchunk, BH), 32, 0, st>>>(labels, S, count, hist, nchunk, a.perm_out);
+    if (it + 1 < a.iterations)
+      grp_update_wide<T, D><<<dim3(count, BH), D, 0, st>>>(v, a.H, S, a.sb, a.sh, a.ss, count, hist, nchunk,
+                                                           a.perm_out, centers);
+  }
+  if (a.labels_out)
+    cudaMemcpyAsync(a.labels_out, labels, BH * S * 4, cudaMemcpyDeviceToDevice, st);
+  if (a.centers_out)
+    cudaMemcpyAsync(a.centers_out, centers, BH * count * D * 4, cudaMemcpyDeviceToDevice, st);
+  return cudaGetLastError() == cudaSuccess ? VC_OK : VC_ERR_LAUNCH;
 }
 
 template <typename T, int D>
@@ -333,21 +460,30 @@ int launch_group(const GroupArgs& a, cudaStream_t st) {
 
 }  // namespace
 
-int64_t group_values_workspace(int64_t B, int64_t H, int64_t S, int64_t D, int) {
+int64_t group_values_workspace(int64_t B, int64_t H, int64_t S, int64_t D, int clusters) {
   const int64_t BH = B * H, tiles = (S + kRows - 1) / kRows, nchunk = (S + kChunk - 1) / kChunk;
   auto up = [](int64_t x) { return ((x + 255) / 256) * 256; };
+  const int64_t count = min64(clusters, S);
+  if (count > kMaxC)   // wide path: centres, labels, sort histogram
+    return up(BH * count * D * 4) + up(BH * S * 4) + up(BH * nchunk * count * 4) + 256;
   return up(BH * kMaxC * D * 4) + up(BH * S * 4) + up(BH * tiles * kMaxC * D * 4) + up(BH * tiles * kMaxC * 4) +
          up(BH * nchunk * kMaxC * 4) + 256;
 }
 
 int group_values(const GroupArgs& a, cudaStream_t st) {
-  if (min64(a.clusters, a.S) > kMaxC) {
-    set_last_error("vc_group_values: more than %d effective clusters is not supported by this build", kMaxC);
-    return VC_ERR_UNSUPPORTED;
+  const bool wide = min64(a.clusters, a.S) > kMaxC;
+  if (a.dtype == VC_DTYPE_BF16) {
+    if (wide) return a.D == 64 ? launch_group_wide<__nv_bfloat16, 64>(a, st) : launch_group_wide<__nv_bfloat16, 128>(a, st);
+    return a.D == 64 ? launch_group<__nv_bfloat16, 64>(a, st) : launch_group<__nv_bfloat16, 128>(a, st);
   }
-  if (a.dtype == VC_DTYPE_BF16) return a.D == 64 ? launch_group<__nv_bfloat16, 64>(a, st) : launch_group<__nv_bfloat16, 128>(a, st);
-  if (a.dtype == VC_DTYPE_F16) return a.D == 64 ? launch_group<__half, 64>(a, st) : launch_group<__half, 128>(a, st);
-  if (a.dtype == VC_DTYPE_F32) return a.D == 64 ? launch_group<float, 64>(a, st) : launch_group<float, 128>(a, st);
+  if (a.dtype == VC_DTYPE_F16) {
+    if (wide) return a.D == 64 ? launch_group_wide<__half, 64>(a, st) : launch_group_wide<__half, 128>(a, st);
+    return a.D == 64 ? launch_group<__half, 64>(a, st) : launch_group<__half, 128>(a, st);
+  }
+  if (a.dtype == VC_DTYPE_F32) {
+    if (wide) return a.D == 64 ? launch_group_wide<float, 64>(a, st) : launch_group_wide<float, 128>(a, st);
+    return a.D == 64 ? launch_group<float, 64>(a, st) : launch_group<float, 128>(a, st);
+  }
   return VC_ERR_ARG;
 }
 

@@ -32,6 +32,7 @@ enum : uint32_t {
   kErrTmemAlloc = 1u << 5,
   kErrBadArgument = 1u << 6,
   kErrBadIndex = 1u << 7,     // a permutation entry outside [0, S): that row read as zeros
+  kErrTimeoutSelfTest = 1u << 8,   // vc_selftest_wait_timeout: its wait gave up, as intended
 };
 
 __device__ __forceinline__ void raise_error(uint32_t bits) { atomicOr(&g_error_word, bits); }
@@ -173,16 +174,52 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // hardware honours the suspend hint or returns early.
 constexpr uint64_t kWaitBudgetNs = 2000000000ull;
 constexpr uint32_t kSuspendHintNs = 100000;
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t err) {
+// mbar_wait with an explicit budget (the self-test uses a short one).
+__device__ __forceinline__ bool mbar_wait_budget(uint64_t* bar, uint32_t parity, uint32_t err, uint64_t budget_ns) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint32_t hint = budget_ns < kSuspendHintNs ? static_cast<uint32_t>(budget_ns) : kSuspendHintNs;
   for (;;) {
-    if (mbar_try_wait_for(a, parity, kSuspendHintNs)) return true;
-    if (globaltimer_ns() - t0 > kWaitBudgetNs) break;
+    if (mbar_try_wait_for(a, parity, hint)) return true;
+    if (globaltimer_ns() - t0 > budget_ns) break;
   }
   raise_error(err);
   return false;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t err) {
+  return mbar_wait_budget(bar, parity, err, kWaitBudgetNs);
+}
+
+// Non-blocking test of a phase (mbarrier.test_wait).
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait by polling (no suspension, so no wake-up latency once the
+// phase completes; costs issue slots while it waits).  Same 2 s budget.
+__device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity, uint32_t err) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_test(a, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_test(a, parity)) return true;
+    if ((i & 255u) == 0 && globaltimer_ns() - t0 > kWaitBudgetNs) break;
+  }
+  raise_error(err);
+  return false;
+}
+__device__ __forceinline__ bool mbar_spin_warp(uint64_t* bar, uint32_t parity, uint32_t err) {
+  const bool ok = mbar_spin(bar, parity, err);
+  return __all_sync(0xffffffffu, ok);
 }
 
 // Warp-uniform bounded wait: every lane polls, the warp agrees on the result
@@ -300,6 +337,17 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t d, uint64_t adesc, uint64_t 
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
       : "memory");
 }
+// True in exactly one active lane of a converged warp (elect.sync).  MMA
+// issue loops run in the whole warp, so descriptor arithmetic stays
+// warp-uniform, and elect one lane per instruction.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n .reg .b32 rx;\n .reg .pred px;\n elect.sync rx|px, 0xffffffff;\n selp.b32 %0, 1, 0, px;\n}\n"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // D[tmem] (+)= A[smem desc] * B[smem desc], kind::i8 (s32 accumulate).
 __device__ __forceinline__ void mma_i8_ss(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
   asm volatile(

@@ -110,8 +110,8 @@ int expcast_codes(const float* x, uint8_t* y, int64_t n, cudaStream_t st);
 // Tensor-core throughput measurement (tensor_peak.cu): ``ctas`` CTAs, each
 // issuing ``iters`` x 4 MMAs of M=128 x n x K=32 (kind 0: kind::i8, 1: E4M3
 // kind::f8f6f4); ``stamps`` (optional, device, 3 per CTA): issue cycles,
-// completion cycles, ok flag.  ``a_tmem``: A read from tensor memory; ``nacc`` accumulators in turn.
-int tensor_peak(int kind, int n, int64_t iters, int ctas, int a_tmem, int nacc, unsigned long long* stamps,
+// completion cycles, ok flag.  ``a_tmem``: A read from tensor memory; ``issuers`` warps issue concurrently.
+int tensor_peak(int kind, int n, int64_t iters, int ctas, int a_tmem, int issuers, unsigned long long* stamps,
                 cudaStream_t st);
 cudaError_t tensor_peak_error_word(uint32_t* code, bool clear);
 

@@ -90,8 +90,8 @@ class Config:
                 raise ValueError("sm100a requires k_quant_block to be a multiple of 128, at most 4096")
             if self.q_block != 128 or self.kv_block != 128:
                 raise ValueError("sm100a requires q_block=128 and kv_block=128")
-            if self.v_smooth and self.clusters > 8:
-                raise ValueError("sm100a groups V into at most 8 clusters")
+            if self.v_smooth and self.clusters > 256:
+                raise ValueError("sm100a groups V into at most 256 clusters (the grouping kernels' range)")
             if self.mean_dtype != "float16":
                 raise ValueError("sm100a stores block means as float16")
 

@@ -45,6 +45,7 @@ SIGNATURES = {
                                        _i64, _i32, _i32, _i64, _f, _i64, _i64, _p]),
     "vc_kernel_resources": (_i32, [_i32, C.POINTER(C.c_int64)]),
     "vc_tensor_peak": (_i32, [_i32, _i32, _i64, _i32, _i32, _i32, _p, _p]),
+    "vc_selftest_wait_timeout": (_i32, [_i64, _p, _p]),
 }
 
 _lib = None

@@ -269,12 +269,12 @@ def kernel_resources(head_dim: int = 128) -> dict:
 
 
 def tensor_peak(kind: str = "i8", n: int = 256, iters: int = 20000, device=None, repeats: int = 5,
-                a_tmem: bool = False, nacc: int = 1) -> dict:
+                a_tmem: bool = False, issuers: int = 1) -> dict:
     """Measured dense tensor-core rate of this GPU for ``kind`` "i8"
     (tcgen05 kind::i8) or "e4m3" (kind::f8f6f4): one CTA per SM issuing
     M=128 x n x K=32 MMAs from shared memory, CUDA-event timed, best of
-    ``repeats`` launches (``a_tmem``: A from tensor memory; ``nacc``
-    independent accumulators used in turn).  Returns TOPS
+    ``repeats`` launches (``a_tmem``: A from tensor memory; ``issuers``
+    warps issuing at once, each into its own accumulator).  Returns TOPS
     and the issue/completion cycles per MMA instruction of CTA 0."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
@@ -287,7 +287,7 @@ def tensor_peak(kind: str = "i8", n: int = 256, iters: int = 20000, device=None,
         for _ in range(repeats + 1):
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(st)
-            N.check(lib.vc_tensor_peak(k, int(n), int(iters), sms, int(bool(a_tmem)), int(nacc), _p(stamps),
+            N.check(lib.vc_tensor_peak(k, int(n), int(iters), sms, int(bool(a_tmem)), int(issuers), _p(stamps),
                                       st.cuda_stream),
                     "vc_tensor_peak")
             e1.record(st)
@@ -297,10 +297,32 @@ def tensor_peak(kind: str = "i8", n: int = 256, iters: int = 20000, device=None,
     s = stamps.view(sms, 3).cpu()
     if not bool((s[:, 2] == 1).all()):
         raise RuntimeError("vc_tensor_peak: a CTA's completion wait timed out")
-    ops_total = 2.0 * 128 * n * 32 * 4 * iters * sms
+    ops_total = 2.0 * 128 * n * 32 * 4 * iters * issuers * sms
     n_mma = 4 * iters
     return {"kind": kind, "n": n, "tops": ops_total / (best * 1e-3) / 1e12, "ms": best, "ctas": sms,
             "issue_cycles_per_mma": float(s[0, 0]) / n_mma, "cycles_per_mma": float(s[0, 1]) / n_mma}
+
+
+ERR_WAIT_SELFTEST = 0x100
+
+
+def wait_timeout_selftest(budget_ns: int = 5_000_000, device=None) -> dict:
+    """Make a device wait run out on purpose: one warp waits, through the
+    bounded mbarrier wait all kernels use, for a phase nothing completes.
+    Returns whether the wait reported success (it must not), the kernel's
+    duration and the device error word read afterwards (bit 0x100 set, then
+    cleared)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    flag = torch.full((1,), -1, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        st = torch.cuda.current_stream(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        N.check(N.load().vc_selftest_wait_timeout(int(budget_ns), _p(flag), st.cuda_stream),
+                "vc_selftest_wait_timeout")
+        e1.record(st)
+        e1.synchronize()
+    return {"wait_ok": int(flag.item()), "ms": e0.elapsed_time(e1), "error_word": error_word(dev.index, clear=True)}
 
 
 def error_word(device: int = 0, clear: bool = True) -> int:

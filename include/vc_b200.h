@@ -55,7 +55,7 @@ const char* vc_last_error(void);
  * optionally clears it.  Bits: 0x01-0x10 a bounded wait gave up (TMA, MMA,
  * softmax, correction, producer), 0x20 tensor-memory allocation, 0x40 a bad
  * kernel argument, 0x80 a permutation entry outside [0, S) (that row was read
- * as zeros).
+ * as zeros), 0x100 the wait of vc_selftest_wait_timeout gave up (as intended).
  * Replaces: no reference counterpart (the reference spins without bound,
  * third_party/sageattention_local/csrc/vc/vc_sm90.cu:114-128). */
 int vc_error_read(int device, uint32_t* code, int clear);
@@ -190,6 +190,15 @@ int vc_attention_fwd_e4m3qk(const uint8_t* q8, const float* qs, const uint8_t* k
                             int64_t k_quant_block, float sm_scale, int64_t unit_begin, int64_t unit_end,
                             void* stream);
 
+/* Failure-detection self-test (no counterpart in the reference, whose
+ * kernels wait without bound, csrc/vc/vc_sm90.cu:114-128): one warp waits,
+ * through the same bounded mbarrier wait every kernel here uses, for a
+ * phase that nothing completes.  After ``budget_ns`` (1e3..2e9) it gives up,
+ * sets bit 0x100 in the device error word (vc_error_read) and
+ * returns; the context stays usable.  ``ok_out`` (optional, device int)
+ * receives 0 (gave up) or 1. */
+int vc_selftest_wait_timeout(int64_t budget_ns, int* ok_out, void* stream);
+
 /* Compiled resources of the fused kernel (registers/thread, static+dynamic
  * shared bytes, threads) for head_dim 64/128 into out[0..3].
  * Replaces _vc_sm90.kernel_resources (csrc/vc/vc_sm90.cu:788-822). */
@@ -201,13 +210,13 @@ int vc_kernel_resources(int head_dim, int64_t* out4);
  * SM) that each issue iters x 4 MMAs of M=128, N=n, K=32 from shared-memory
  * operands: kind 0 = tcgen05 kind::i8 (s32 accumulate), kind 1 = kind::f8f6f4
  * with E4M3 operands (f32 accumulate); ``a_tmem`` != 0 reads A from tensor
- * memory instead of shared memory; the MMAs accumulate into ``nacc``
- * accumulators in turn (nacc * ceil(n/32)*32 columns must fit in 512, or in
- * 448 with A in tensor memory).  ``stamps`` (optional, device, 3 per
+ * memory instead of shared memory; ``issuers`` warps (1-4) issue at once,
+ * each into its own accumulator (issuers * ceil(n/32)*32 columns must fit in
+ * 512, or in 448 with A in tensor memory).  ``stamps`` (optional, device, 3 per
  * CTA) receives the issue and completion cycles and an ok flag.  The caller
- * times the launch (ops = 2*128*n*32*4*iters*ctas).  n in [16,256] step 16,
+ * times the launch (ops = 2*128*n*32*4*iters*issuers*ctas).  n in [16,256] step 16,
  * iters in [1, 2^22]. */
-int vc_tensor_peak(int kind, int n, int64_t iters, int ctas, int a_tmem, int nacc, unsigned long long* stamps,
+int vc_tensor_peak(int kind, int n, int64_t iters, int ctas, int a_tmem, int issuers, unsigned long long* stamps,
                    void* stream);
 
 #ifdef __cplusplus

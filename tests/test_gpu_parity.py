@@ -208,7 +208,10 @@ def test_v_blocks_many_tiles_channel_reduction(ops):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("dim", [64, 128])
-@pytest.mark.parametrize("n,count,iterations", [(1, 8, 2), (127, 3, 3), (129, 8, 2), (2049, 8, 2)])
+@pytest.mark.parametrize("n,count,iterations", [(1, 8, 2), (127, 3, 3), (129, 8, 2), (2049, 8, 2),
+                                                # the wide path (9-256 effective centres)
+                                                (1000, 16, 2), (300, 64, 3), (2049, 256, 2), (100, 200, 2),
+                                                (20, 256, 1)])
 def test_group_values_matches_fp64_lloyd(ops, dtype, dim, n, count, iterations):
     # well-separated clusters, as scripts/validate_sage_vc.py:86-117
     g = torch.Generator().manual_seed(883)
@@ -231,10 +234,12 @@ def test_group_values_stable_known_answer_and_constant(ops):
     for p in _np(perm).reshape(-1, 6):
         assert p.tolist() == [0, 3, 2, 4, 1, 5]
     v = torch.full((2, 2, 257, 128), 2.)
-    perm, lab, centers = ops.group_values(v.cuda(), 8, 3, debug=True)
-    assert int(lab.count_nonzero()) == 0
-    assert torch.equal(perm.cpu(), torch.arange(257).expand(2, 2, 257))
-    assert bool((centers == 2).all())
+    for count in (8, 100):   # fused and wide paths: all tokens tie, the lowest centre wins
+        perm, lab, centers = ops.group_values(v.cuda(), count, 3, debug=True)
+        assert int(lab.count_nonzero()) == 0
+        assert torch.equal(perm.cpu(), torch.arange(257).expand(2, 2, 257))
+        assert bool((centers == 2).all())
+
 
 
 def _device_state(ops, q, k, v, *, expcast=True, v_smooth=False, v_scale_mode="channel", perm=None):
@@ -426,6 +431,35 @@ def test_sageattn_vc_end_to_end_and_nhd(ops):
     assert torch.equal(nhd.transpose(1, 2), out)
     dense = O.dense_attention(q, k, v)
     print("vs dense fp32:", O.metrics(out.float().cpu(), dense))
+
+
+@pytest.mark.parametrize("clusters", [16, 64, 256])
+def test_sageattn_vc_wide_grouping_end_to_end(ops, clusters):
+    """sageattn_vc with 9-256 clusters (the reference's public range beyond
+    its fused 8-cluster path): on clustered V whose linspace-initial tokens
+    lie in distinct clusters (so Lloyd has no ties), the device labels equal
+    the FP64 Lloyd oracle's and the permutation is their stable argsort; the
+    output equals the oracle's on the same permutation within the parity
+    tolerance."""
+    from sageattention_local import sageattn_vc
+    n = 1100
+    shape = (1, 2, n, 128)
+    g = torch.Generator().manual_seed(90 + clusters)
+    q, k, _ = qk_inputs(90 + clusters, shape, torch.bfloat16, 3 ** 0.5)
+    lab = torch.randint(0, clusters, (n,), generator=g)
+    lab[torch.from_numpy(O.linspace_ids(n, clusters))] = torch.arange(clusters)
+    centres = torch.randn(1, 2, clusters, 128, generator=g) * 3
+    v = (centres[:, :, lab] + 0.05 * torch.randn(shape, generator=g)).to(torch.bfloat16)
+    perm, labels, _ = ops.group_values(v.cuda(), clusters, 2, debug=True)
+    e_lab, _ = O.lloyd_fp64(v.float().numpy(), clusters, 2)
+    assert np.array_equal(_np(labels), e_lab)
+    assert np.array_equal(_np(perm), O.stable_argsort(e_lab))
+    out = sageattn_vc(q.cuda(), k.cuda(), v.cuda(), v_smooth=True, clusters=clusters)
+    torch.cuda.synchronize()
+    kk = k.gather(2, perm.cpu().unsqueeze(-1).expand_as(k))
+    ref = O.reference(O.prepare(q, k, v, v_smooth=True, permutation=perm.cpu(), km=O.k_mean(kk)))
+    m = O.metrics(out.float().cpu(), ref)
+    assert m["cos"] >= 0.9999 and m["rel_l2"] <= 4e-3, m
 
 
 def test_sageattn_vc_smooth_end_to_end(ops):

@@ -41,7 +41,7 @@ def test_config_defaults_match_the_reference():
     ({"backend": "sm100a", "qk_hadamard": False, "quantize": False}, "quantize"),
     ({"backend": "sm100a", "qk_hadamard": False, "q_block": 64}, "q_block=128"),
     ({"backend": "sm100a", "qk_hadamard": False, "kv_block": 256, "k_quant_block": 256}, "kv_block=128"),
-    ({"backend": "sm100a", "qk_hadamard": False, "v_smooth": True, "clusters": 9}, "8 clusters"),
+    ({"backend": "sm100a", "qk_hadamard": False, "v_smooth": True, "clusters": 257}, "256 clusters"),
     ({"backend": "sm100a", "qk_hadamard": False, "mean_dtype": "bfloat16"}, "float16"),
 ])
 def test_config_rejects(kwargs, match):
@@ -52,6 +52,7 @@ def test_config_rejects(kwargs, match):
 def test_sm100a_config_accepts_its_contract():
     c = Config(backend="sm100a", qk_hadamard=False, expcast=True, v_smooth=True)
     assert c.backend == "sm100a"
+    assert Config(backend="sm100a", qk_hadamard=False, v_smooth=True, clusters=256).clusters == 256
 
 
 def _qkv(shape=(1, 2, 5, 64), dtype=torch.float16):
