@@ -13,26 +13,38 @@
 // Warp roles (384 threads):
 //   warps 0-3   softmax group A (tile A), thread t owns row t = TMEM lane t
 //   warps 4-7   softmax group B (tile B)
-//   warp 8      Q (both tiles, once) and K producer (TMA, 4-deep ring)
+//   warp 8      K producer (TMA, 4-deep ring) [+ both Q tiles once at D = 128]
 //   warp 9      TMEM allocator + QK^T issuer: QK_A(j), QK_B(j), QK_A(j+1), ...
 //   warp 10     V producer (3-deep ring) [+ the block means operand]
 //   warp 11     P.V issuer: PV_A(j), PV_B(j), PV_A(j+1), ... [+ means MMAs]
+// The issuers run their loops in the whole warp (descriptor arithmetic stays
+// warp-uniform) and one elected lane issues each MMA and commit.
 //
-// Q is staged in shared memory by TMA and QK^T reads both operands from
-// shared memory (kind::i8, or kind::f8f6f4 for E4M3 block Q/K).  Before each
+// QK^T is kind::i8 (kind::f8f6f4 for E4M3 block Q/K).  At D = 64, Q lives in
+// tensor memory (each softmax thread stores its own row) and QK^T reads only
+// K from shared memory: measured on B200, an M=128 N=128 K=32 MMA takes about
+// 73 cycles with A in tensor memory and about 103 with both operands in
+// shared memory.  At D = 128 there is no room for Q in tensor memory next to
+// P, and P there is worth more (moving P to shared memory to make room was
+// measured 3% slower), so Q is staged in shared memory by TMA.  Before each
 // INT8 QK^T one kind::f16 MMA presets the score slot to the bits of 1.5*2^23
-// (2048 x 6144 from constant operands), so s32 scores read back as the
-// floats 1.5*2^23 + s.
+// (2048 x 6144 from constant operands; at D = 128 the A operand sits in
+// tensor memory), so s32 scores read back as the floats 1.5*2^23 + s.
 //
 // Tensor memory (512 columns):
 //   D = 128: S [0,128) one score slot, used in the order A(0), B(0), A(1), ...
-//            O_A [128,272)  O_B [288,432)  P_A [448,480)  P_B [480,512)
+//            O_A [128,272)  O_B [288,432)  preset A operand [432,440)
+//            P_A [448,480)  P_B [480,512);  Q_A, Q_B in shared memory
 //   D = 64:  S_A [0,128) S_B [128,256)   one slot per tile
-//            O_A [256,336)  O_B [352,432)  P_A [448,480)  P_B [480,512)
+//            O_A [256,336)  O_B [336,416)  Q_A [416,432)  Q_B [432,448)
+//            P_A [448,480)  P_B [480,512)
+// At D = 128 a second score slot does not fit, so QK^T issue n = 2j + X uses
+// slot n % NS and may overwrite it once the scores of issue n - NS have been
+// read; that round trip (issuer wake-up, preset and QK^T MMAs, group
+// wake-up, score read) bounds the tile period there.
 // O_X holds D FP32 output columns plus a 16-column block whose first column
 // accumulates P.1 (the ExpCast denominator) through a row of E4M3 1.0
-// appended to every V tile.  QK^T issue n = 2j + X uses slot n % NS and may
-// overwrite it once the scores of issue n - NS have been read.
+// appended to every V tile.
 //
 // Block means (V smoothing, channel scales): O_X needs mass_t * mean_t/s per
 // tile besides P.V.  The mass of tile t is the growth of the denominator
@@ -62,16 +74,21 @@ constexpr int kPVS = 3;   // V ring depth
 template <int D>
 struct PairCols {
   static constexpr int kNS = D == 64 ? 2 : 1;                 // score slots
+  static constexpr bool kQTmem = D == 64;                     // Q in tensor memory (else shared, by TMA)
+  static constexpr bool kPresetTmem = D == 128;               // preset A operand in tensor memory
   static constexpr uint32_t kS = 0;                           // slot s at kS + 128 s
   static constexpr uint32_t kOA = D == 64 ? 256 : 128;
-  static constexpr uint32_t kOB = D == 64 ? 352 : 288;
+  static constexpr uint32_t kOB = D == 64 ? 336 : 288;
+  static constexpr uint32_t kQA = 416, kQB = 432;             // D = 64 only
   static constexpr uint32_t kPA = 448, kPB = 480;
-  static_assert(kOA + D + 16 <= kOB && kOB + D + 16 <= kPA, "tensor-memory columns overlap");
+  static constexpr uint32_t kPresetA = 432;                   // D = 128 only
+  static_assert(kOA + D + 16 <= kOB && kOB + D + 16 <= (D == 64 ? kQA : kPresetA), "tensor-memory columns overlap");
 };
 
 struct __align__(8) PairBarriers {
   uint64_t k_full[kPKS], k_empty[kPKS], v_full[kPVS], v_empty[kPVS];
-  uint64_t q_full;
+  uint64_t q_ready[2];     // Q in tensor memory: tile X's rows stored (count 128)
+  uint64_t q_full;         // Q in shared memory: both tiles loaded (TMA)
   uint64_t s_full[2], s_free[2], p_full[2], pv_done[2], o_final[2];
   uint64_t mean_full[2];   // block means: batch buffer k%2 of the means operand written
   uint64_t a_full[2];      // block means: tile X's mass operand of a batch written (count 128)
@@ -79,13 +96,13 @@ struct __align__(8) PairBarriers {
 
 template <int D>
 struct PairSmem {
-  static constexpr int kK = 128 * D;              // K stage (and one Q tile)
+  static constexpr int kK = 128 * D;              // K stage
   static constexpr int kV = (D + 16) * 128;       // V^T rows + ones row + zero rows
   static constexpr int kOffK = 0;
   static constexpr int kOffV = kOffK + kPKS * kK;
-  static constexpr int kOffQ = kOffV + kPVS * kV;                 // Q_A, Q_B
+  static constexpr int kOffQ = kOffV + kPVS * kV;                 // Q_A, Q_B (Q in shared memory)
+  static constexpr int kOffMassA = kOffQ + (PairCols<D>::kQTmem ? 0 : 2 * kK);
   static constexpr int kMassA = 128 * 32;                         // 128 x 16 FP16 per tile
-  static constexpr int kOffMassA = kOffQ + 2 * kK;                // two mass operands (A, B)
   static constexpr int kMean = D * 32;                            // D x 16 FP16
   static constexpr int kOffMean = kOffMassA + 2 * kMassA;         // two batch buffers
   static constexpr int kOffPresetA = kOffMean + 2 * kMean;
@@ -94,6 +111,7 @@ struct PairSmem {
   static constexpr int kOffSlot = kOffBar + int(sizeof(PairBarriers));
   static constexpr int kBytes = kOffSlot + 16;
   static constexpr int kAlloc = kBytes + 1024;
+  static_assert(kOffQ % 1024 == 0, "Q tiles need 1024-byte alignment (128-byte swizzle)");
   static_assert(kAlloc <= 227 * 1024, "shared memory");
 };
 
@@ -140,8 +158,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       mbar_init(&bar->v_full[s], 1);
       mbar_init(&bar->v_empty[s], 1);
     }
-    mbar_init(&bar->q_full, 1);
     for (int x = 0; x < 2; ++x) {
+      mbar_init(&bar->q_ready[x], 128);
       mbar_init(&bar->s_full[x], 1);
       mbar_init(&bar->s_free[x], 128);
       mbar_init(&bar->p_full[x], 128);
@@ -150,6 +168,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       mbar_init(&bar->mean_full[x], 32);
       mbar_init(&bar->a_full[x], 128);
     }
+    mbar_init(&bar->q_full, 1);
     fence_barrier_init();
   }
   for (int i = threadIdx.x; i < kPVS * 16 * 8; i += kPairThreads) {
@@ -173,7 +192,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     tmem_relinquish();
   }
   if (warp == 8 && lane == 0) {
-    tma_prefetch_desc(&tmq);
+    if constexpr (!C::kQTmem) tma_prefetch_desc(&tmq);
     tma_prefetch_desc(&tmk);
   }
   if (warp == 10 && lane == 0) tma_prefetch_desc(&tmv);
@@ -185,12 +204,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   if (warp >= 8) {
     setmaxnreg_dec<56>();
     if (warp == 8 && lane == 0) {
-      // ------------------------------------------------------- Q, K producer
-      // a tile B past the end of the head reads as zeros (its rows are never written)
-      mbar_expect_tx(&bar->q_full, 2 * L::kK);
-      tma_load_3d(smem + L::kOffQ, &tmq, &bar->q_full, 0, static_cast<int>(qt0 * 128), static_cast<int>(bh));
-      tma_load_3d(smem + L::kOffQ + L::kK, &tmq, &bar->q_full, 0, static_cast<int>(qt0 * 128 + 128),
-                  static_cast<int>(bh));
+      // ---------------------------------------------------------- K producer
+      if constexpr (!C::kQTmem) {
+        // both Q tiles; a tile B past the end of the head reads as zeros (its rows are never written)
+        mbar_expect_tx(&bar->q_full, 2 * L::kK);
+        tma_load_3d(smem + L::kOffQ, &tmq, &bar->q_full, 0, static_cast<int>(qt0 * 128), static_cast<int>(bh));
+        tma_load_3d(smem + L::kOffQ + L::kK, &tmq, &bar->q_full, 0, static_cast<int>(qt0 * 128 + 128),
+                    static_cast<int>(bh));
+      }
       for (int j = 0; j < T; ++j) {
         const int s = j % kPKS;
         if (j >= kPKS && !mbar_wait(&bar->k_empty[s], ((j / kPKS) & 1) ^ 1, kErrTimeoutProducer)) break;
@@ -246,9 +267,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       }
     } else if (warp == 9) {
       // ------------------------------------------------------- QK^T issuer
-      // issue n = 2j + X into slot n % NS once the scores of issue n - NS are
-      // read.  The loop runs in the whole warp (descriptor arithmetic stays
-      // warp-uniform) and one elected lane issues each MMA and commit.
+      // issue n = 2j + X into slot n % NS once the scores of issue n - NS are read
       constexpr uint32_t idesc_qk = QF8 ? idesc_make(1, 0, 0, 128, 128) : idesc_make(2, 1, 1, 128, 128);
       constexpr uint32_t idesc_preset = idesc_make(1, 0, 0, 128, 128);   // f32 <- f16 x f16
       const uint64_t adesc_preset = smem_desc_plain(smem_u32(smem + L::kOffPresetA), 128, 256);
@@ -256,7 +275,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       const uint64_t kdesc0 = kmajor_desc<D>(smem_u32(smem + L::kOffK));
       const uint64_t qdesc0 = kmajor_desc<D>(smem_u32(smem + L::kOffQ));
       constexpr uint64_t kStep = (L::kK >> 4);   // descriptor start-address units per K stage / Q tile
-      bool ok = mbar_wait_warp(&bar->q_full, 0, kErrTimeoutMma);
+      bool ok = mbar_wait_warp(&bar->q_ready[0], 0, kErrTimeoutMma) && mbar_wait_warp(&bar->q_ready[1], 0, kErrTimeoutMma);
+      if constexpr (!C::kQTmem) ok = ok && mbar_wait_warp(&bar->q_full, 0, kErrTimeoutMma);
       for (int j = 0; j < T && ok; ++j) {
         const int s = j % kPKS;
         if (!mbar_wait_warp(&bar->k_full[s], (j / kPKS) & 1, kErrTimeoutMma)) break;
@@ -270,15 +290,24 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           }
           tc_fence_after();
           const uint32_t scol = tmem + C::kS + 128 * (n % C::kNS);
+          const uint32_t qcol = tmem + (x ? C::kQB : C::kQA);
           const uint64_t qd = qdesc0 + x * kStep;
           if (elect_one()) {
-            if constexpr (QF8) {
+            if constexpr (!QF8) {
+              // S = the bits of 1.5*2^23, then QK^T accumulates onto it
+              if constexpr (C::kPresetTmem) mma_f16_ts(scol, tmem + C::kPresetA, bdesc_preset, idesc_preset, 0u);
+              else mma_f16_ss(scol, adesc_preset, bdesc_preset, idesc_preset, 0u);
+            }
 #pragma unroll
-              for (int kk = 0; kk < D / 32; ++kk) mma_f8_ss(scol, qd + 2 * kk, kd + 2 * kk, idesc_qk, kk > 0 ? 1u : 0u);
-            } else {
-              mma_f16_ss(scol, adesc_preset, bdesc_preset, idesc_preset, 0u);   // S = the bits of 1.5*2^23
-#pragma unroll
-              for (int kk = 0; kk < D / 32; ++kk) mma_i8_ss(scol, qd + 2 * kk, kd + 2 * kk, idesc_qk, 1u);
+            for (int kk = 0; kk < D / 32; ++kk) {
+              const uint32_t acc = QF8 ? (kk > 0 ? 1u : 0u) : 1u;
+              if constexpr (C::kQTmem) {
+                if constexpr (QF8) mma_f8_ts(scol, qcol + kk * 8, kd + 2 * kk, idesc_qk, acc);
+                else mma_i8_ts(scol, qcol + kk * 8, kd + 2 * kk, idesc_qk, acc);
+              } else {
+                if constexpr (QF8) mma_f8_ss(scol, qd + 2 * kk, kd + 2 * kk, idesc_qk, acc);
+                else mma_i8_ss(scol, qd + 2 * kk, kd + 2 * kk, idesc_qk, acc);
+              }
             }
             mma_commit(&bar->s_full[x]);
           }
@@ -290,7 +319,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       }
     } else if (warp == 11) {
       // ---------------------------------------------------------- P.V issuer
-      // (whole warp, one elected lane per MMA and commit, as above)
       constexpr uint32_t idesc_pv = idesc_make(1, 0, 0, 128, D + 16);  // f32 <- e4m3 x e4m3
       constexpr uint32_t idesc_mean = idesc_make(1, 0, 0, 128, D);     // f32 <- f16 x f16
       const uint64_t vdesc0 = smem_desc_sw128(smem_u32(smem + L::kOffV));
@@ -312,8 +340,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           }
           tc_fence_after();
           const uint32_t ocol = tmem + (x ? C::kOB : C::kOA);
-          const uint32_t pcol = tmem + (x ? C::kPB : C::kPA);
           if (elect_one()) {
+            const uint32_t pcol = tmem + (x ? C::kPB : C::kPA);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
               mma_f8_ts(ocol, pcol + kk * 8, vd + 2 * kk, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
@@ -372,7 +400,28 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const bool write_row = row_valid && unit >= p.unit_begin && unit < p.unit_end;
     const uint32_t scol = tmem + lane_base + C::kS + 128 * (C::kNS == 2 ? x : 0);
     const uint32_t ocol = tmem + lane_base + (x ? C::kOB : C::kOA);
-    const uint32_t pcol = tmem + lane_base + (x ? C::kPB : C::kPA);
+    {
+      if constexpr (C::kQTmem) {
+        // this row of Q into tensor memory (the A operand of QK^T); rows past Sq are zeros
+        uint32_t qw[D / 4];
+        const int8_t* qrow = p.q8 + (bh * p.Sq + (row_valid ? row : 0)) * D;
+#pragma unroll
+        for (int i = 0; i < D / 16; ++i) {
+          const uint4 u = row_valid ? __ldg(reinterpret_cast<const uint4*>(qrow) + i) : make_uint4(0, 0, 0, 0);
+          qw[4 * i] = u.x; qw[4 * i + 1] = u.y; qw[4 * i + 2] = u.z; qw[4 * i + 3] = u.w;
+        }
+        tmem_st16(tmem + lane_base + (x ? C::kQB : C::kQA), qw);
+      }
+      if constexpr (C::kPresetTmem) {
+        if (x == 0) {   // the preset's A operand: FP16 2048 in K element 0 of every row
+          const uint32_t pre[8] = {0x6800u, 0, 0, 0, 0, 0, 0, 0};
+          tmem_st8(tmem + lane_base + C::kPresetA, pre);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bar->q_ready[x]);
+    }
     // INT8: the Sage per-thread Q scale of the row; E4M3 blocks: one scale per 128-row Q tile
     const float qscale = !row_valid ? 0.f : QF8 ? p.qs[bh * p.nqs + qt] : p.qs[bh * p.nqs + (row >> 4) * 8 + (row & 7)];
     const float scale = p.sm_scale;
@@ -509,7 +558,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         tmem_st1(ocol + D, __float_as_uint(__fmul_rn(__uint_as_float(draw), alpha)));
       }
       tc_fence_after();
-      tmem_st32(pcol, pw);
+      tmem_st32(tmem + lane_base + (x ? C::kPB : C::kPA), pw);
       tmem_wait_st();
       if constexpr (BV) tmem_wait_ld_reg(draw);   // the column read completes before PV_X(j) may start
       tc_fence_before();
