@@ -50,6 +50,9 @@ CONFIGS = {
            "BNSD [2,40,75600,128] bf16, V ~ N(0,1), ExpCast + V grouping + block smoothing"),
 }
 METRIC = "TOPS (4*B*H*S^2*D per call) at BNSD [1,28,37741,128] D128, sageattn_vc ExpCast (prep + fused kernel)"
+# DRAM bytes (read + write) of one full config-2 launch of the paired-tile kernel, from ncu
+# (profiles/vc_attention_pair_kernel_c2_dram.txt)
+TRAFFIC_C2_BYTES = 530e6
 
 
 def peaks():
@@ -383,17 +386,23 @@ def main():
     rows_local = sum(min(128, S - (u % sh.qtiles) * 128) for u in range(sh.unit_begin, sh.unit_end))
     ops_launch = 4.0 * rows_local * S * D
     hbm, bf16, bf16_sus, basis = peaks()
-    peak_tops = 2.0 * bf16          # dense INT8/FP8 tensor rate is 2x the measured dense BF16 rate
+    # dense INT8 rate of this GPU, measured now by this library's own probe (tcgen05 kind::i8,
+    # A in tensor memory, N=256: the fastest form); the peak is the lower of it and 2 x bf16
+    i8 = ops.tensor_peak("i8", 256, iters=20000, a_tmem=True)
+    peak_tops = min(i8["tops"], 2.0 * bf16)
     achieved = ops_launch / (att_ms * 1e-3) / 1e12
-    # DRAM bytes per launch: dram__bytes_read.sum + dram__bytes_write.sum of the alternating-tile
-    # kernel captured by ncu on the full config-2 launch (409.5 MB + 237.7 MB; profiles/
-    # launches_bench_c2.txt), scaled by the heads in this launch; D128, ExpCast, channel-scaled V.
+    # DRAM bytes per launch: dram__bytes_read.sum + dram__bytes_write.sum of the paired-tile kernel
+    # from one ncu capture of the full config-2 launch (profiles/vc_attention_pair_kernel_c2_dram.txt),
+    # scaled by the heads in this launch; D128, ExpCast, channel-scaled V.
     traffic = None
     if D == 128 and not smooth and S == 37741:
-        traffic = 647.2e6 / 28 * nbh
+        traffic = TRAFFIC_C2_BYTES / 28 * nbh
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_tops, "unit": "TFLOP/s",
-                "frac": achieved / peak_tops, "traffic": traffic,
-                "kernel": "vc_attention_alt_kernel", "peak_basis": f"2 x bf16_tflops ({basis}, MEASURED_PEAKS.json)",
+                "frac": achieved / peak_tops, "traffic": traffic, "kernel": "vc_attention_pair_kernel",
+                "peak_basis": (f"min(measured dense INT8 {i8['tops']:.1f} TOPS [vc_tensor_peak: tcgen05 kind::i8, "
+                               f"A in tensor memory, N=256, this run], 2 x bf16_tflops {2.0 * bf16:.1f} "
+                               f"[{basis}, MEASURED_PEAKS.json])"),
+                "peak_i8_measured": i8["tops"], "frac_of_i8_measured": achieved / i8["tops"],
                 "kernel_ms": att_ms, "algorithmic_ops_per_launch": ops_launch}
 
     # end to end through the public API with pinned host buffers

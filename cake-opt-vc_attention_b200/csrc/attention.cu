@@ -59,6 +59,7 @@ struct Params {
   int64_t kq_tiles;   // E4M3 block Q/K: K tiles per K scale
   int64_t unit_begin, unit_end;   // units (b*H+h)*qtiles + q_tile to compute
   int64_t pair_begin, qpairs;     // paired-tile kernel: first pair (b*H+h)*qpairs + q_tile/2, pairs per head
+  int64_t pair_solo_from;         // paired-tile kernel: CTAs from here on take single tiles of the remaining pairs
   float sm_scale;
   int exact_expcast;   // 1: unfused RN(RN(raw*f)-m) encoder instead of the folded affine one
 };
@@ -552,6 +553,19 @@ int dispatch_flags(const AttnArgs& a, const Maps& m, const Params& p, int64_t un
 
 }  // namespace
 
+// Streaming multiprocessors of the current device (cached per device).
+int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
 int attention_fwd(const AttnArgs& a, cudaStream_t st) {
   const int64_t BH = a.B * a.H;
   const int64_t qtiles = (a.Sq + 127) / 128, ktiles = (a.Sk + 127) / 128;
@@ -597,7 +611,12 @@ int attention_fwd(const AttnArgs& a, cudaStream_t st) {
   p.pair_begin = pb;
   p.sm_scale = a.sm_scale;
   p.exact_expcast = a.expcast == 2 ? 1 : 0;
-  const int64_t units = ue - ub, pairs = pe - pb;
+  const int64_t units = ue - ub;
+  // one CTA per SM: if the last wave of pairs would be at most half full, its
+  // pairs run as two single-tile CTAs each (one wave of about half the length)
+  const int64_t npairs = pe - pb, sms = sm_count(), tail = npairs % sms;
+  p.pair_solo_from = tail <= sms / 2 ? npairs - tail : npairs;
+  const int64_t pairs = npairs + (npairs - p.pair_solo_from);   // CTAs of the paired-tile kernel
   if (a.out_dtype == VC_DTYPE_BF16)
     return a.D == 128 ? dispatch_flags<128, __nv_bfloat16>(a, m, p, units, pairs, st)
                       : dispatch_flags<64, __nv_bfloat16>(a, m, p, units, pairs, st);

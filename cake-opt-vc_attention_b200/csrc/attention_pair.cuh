@@ -60,6 +60,12 @@
 // PV_X(8k+8)); the P.V issuer issues its MMA right after PV_X(8k+8) and
 // commits pv_done_X after it, so the next rescale of O follows it.
 //
+// Tail balance.  When the last wave of pair CTAs would be at most half full,
+// the host splits those last pairs into single-tile ("solo") CTAs: tile A only,
+// one chain, one score slot (issue j waits for the read of tile j-1, so no
+// wait can alias a phase two ahead), group B idle.  The tail then costs about
+// one single-tile period instead of a full pair period.
+//
 // Barrier phases.  Every wait is unconditional and taken once per phase in
 // order, and no barrier can complete a phase ahead of its waiter: s_full_X,
 // p_full_X and pv_done_X advance once per tile of chain X, each only after
@@ -144,9 +150,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffSlot);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t pair = p.pair_begin + blockIdx.x;
+  // CTAs [0, pair_solo_from) take pairs pair_begin + i; after them each pair
+  // is split into two solo CTAs (tile A = the pair's first, then second tile)
+  const bool solo = static_cast<int64_t>(blockIdx.x) >= p.pair_solo_from;
+  const int64_t k_solo = static_cast<int64_t>(blockIdx.x) - p.pair_solo_from;
+  const int64_t pair = p.pair_begin + (solo ? p.pair_solo_from + (k_solo >> 1) : static_cast<int64_t>(blockIdx.x));
   const int64_t bh = pair / p.qpairs;
-  const int64_t qt0 = (pair - bh * p.qpairs) * 2;   // tile A; tile B = qt0 + 1
+  const int64_t qt0 = (pair - bh * p.qpairs) * 2 + (solo ? (k_solo & 1) : 0);   // tile A; tile B = qt0 + 1
+  const int nchain = solo ? 1 : 2;
   const int T = static_cast<int>(p.ktiles);
 
   if (threadIdx.x == 0) {
@@ -281,15 +292,18 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const int s = j % kPKS;
         if (!mbar_wait_warp(&bar->k_full[s], (j / kPKS) & 1, kErrTimeoutMma)) break;
         const uint64_t kd = kdesc0 + s * kStep;
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          const int n = 2 * j + x, prev = n - C::kNS;
-          if (prev >= 0 && !mbar_wait_warp(&bar->s_free[prev & 1], (prev >> 1) & 1, kErrTimeoutMma)) {
+        for (int x = 0; x < nchain; ++x) {
+          // pair: issue n = 2j + x into slot n % NS after the read of issue n - NS;
+          // solo: issue j into slot 0 after the read of tile j - 1
+          const int n = solo ? j : 2 * j + x, prev = n - (solo ? 1 : C::kNS);
+          const bool waited = prev < 0 || (solo ? mbar_wait_warp(&bar->s_free[0], prev & 1, kErrTimeoutMma)
+                                                : mbar_wait_warp(&bar->s_free[prev & 1], (prev >> 1) & 1, kErrTimeoutMma));
+          if (!waited) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t scol = tmem + C::kS + 128 * (n % C::kNS);
+          const uint32_t scol = tmem + C::kS + (solo ? 0u : 128u * (n % C::kNS));
           const uint32_t qcol = tmem + (x ? C::kQB : C::kQA);
           const uint64_t qd = qdesc0 + x * kStep;
           if (elect_one()) {
@@ -332,8 +346,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const int s = j % kPVS;
         if (!mbar_wait_warp(&bar->v_full[s], (j / kPVS) & 1, kErrTimeoutMma)) break;
         const uint64_t vd = vdesc0 + s * kStepV;
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
+        for (int x = 0; x < nchain; ++x) {
           if (!mbar_wait_warp(&bar->p_full[x], j & 1, kErrTimeoutMma)) {
             ok = false;
             break;
@@ -367,8 +380,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         if (elect_one()) mma_commit(&bar->v_empty[s]);
         __syncwarp();
       }
-#pragma unroll
-      for (int x = 0; x < 2; ++x) {
+      for (int x = 0; x < nchain; ++x) {
         if constexpr (BV) {
           // the open batch of tile X, written by its group after the loop
           const int kb = (T - 1) >> 3;
@@ -428,7 +440,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const uint64_t bias2 = pk2f(kBias, kBias);
     const uint64_t tiny2 = pk2(kDenormOne, kDenormOne);
     const uint64_t expa2 = pk2f(kExpA, kExpA), expb2 = pk2f(kExpB, kExpB);
-    bool ok = true;
     // K scales of a tile: INT8 four groups (index tile*4 + (key%8)/2); E4M3 blocks one scale per kq_tiles tiles
     auto load_ks = [&](int jj) -> float4 {
       if constexpr (QF8) {
@@ -445,7 +456,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
     for (int i = 0; i < 8; ++i) pend[i] = 0.f;
     uint8_t* massa = smem + L::kOffMassA + x * L::kMassA;
-    for (int j = 0; j < T; ++j) {
+    bool ok = x < nchain;   // group B of a solo CTA has no tile
+    for (int j = 0; ok && j < T; ++j) {
       const float4 ksv = ksv_next;
       if (j + 1 < T) ksv_next = load_ks(j + 1);
       ok = mbar_wait_warp(&bar->s_full[x], j & 1, kErrTimeoutSoftmax);
