@@ -62,6 +62,7 @@ struct Params {
   int64_t pair_solo_from;         // paired-tile kernel: CTAs from here on take single tiles of the remaining pairs
   float sm_scale;
   int exact_expcast;   // 1: unfused RN(RN(raw*f)-m) encoder instead of the folded affine one
+  float ctl_offset;    // FP8-P control: P = e4m3(exp2(logit - max + offset)); 8.807 Sage, 8 the Config contract
 };
 
 struct __align__(8) Barriers {
@@ -96,7 +97,10 @@ __device__ __forceinline__ __nv_bfloat16 to_out<__nv_bfloat16>(float x) { return
 template <>
 __device__ __forceinline__ float to_out<float>(float x) { return x; }
 
-template <int D, typename OutT, bool EXPCAST, bool BLOCK_VALUES, bool VS_PER_BLOCK>
+// QF8: E4M3 block Q/K (the Config contract's Hadamard path): QK^T is
+// kind::f8f6f4 into FP32, the Q scale is one per 128-row tile and the K scale
+// one per kq_tiles K tiles; logits are raw * RN(scale * RN(qs * ks)) on every tile.
+template <int D, typename OutT, bool EXPCAST, bool BLOCK_VALUES, bool VS_PER_BLOCK, bool QF8 = false>
 __global__ void __launch_bounds__(kThreads, 1)
     vc_attention_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, Params p) {
   using L = Smem<D>;
@@ -162,7 +166,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc_qk = idesc_make(2, 1, 1, 128, 128);  // s32 <- s8 x s8
+      constexpr uint32_t idesc_qk = QF8 ? idesc_make(1, 0, 0, 128, 128)     // f32 <- e4m3 x e4m3
+                                        : idesc_make(2, 1, 1, 128, 128);    // s32 <- s8 x s8
       constexpr uint32_t idesc_pv = idesc_make(1, 0, 0, 128, D);    // f32 <- e4m3 x e4m3
       bool ok = mbar_wait(&bar->q_ready, 0, kErrTimeoutMma);
       tc_fence_after();
@@ -195,7 +200,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint64_t desc;
           if constexpr (D == 128) desc = smem_desc_sw128(kaddr + kk * 32);
           else desc = smem_desc_sw64(kaddr + kk * 32);
-          mma_i8_ts(tmem + scol, tmem + kColQ + kk * 8, desc, idesc_qk, kk > 0);
+          if constexpr (QF8) mma_f8_ts(tmem + scol, tmem + kColQ + kk * 8, desc, idesc_qk, kk > 0);
+          else mma_i8_ts(tmem + scol, tmem + kColQ + kk * 8, desc, idesc_qk, kk > 0);
         }
         mma_commit(&bar->k_empty[s]);
         mma_commit(&bar->s_full[j & 1]);
@@ -226,7 +232,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(&bar->q_ready);
     }
-    const float qscale = row_valid ? p.qs[bh * p.nqs + (row >> 4) * 8 + (row & 7)] : 0.f;
+    const float qscale =
+        row_valid ? (QF8 ? p.qs[bh * p.nqs + qt] : p.qs[bh * p.nqs + (row >> 4) * 8 + (row & 7)]) : 0.f;
     const float scale = EXPCAST ? p.sm_scale : __fmul_rn(p.sm_scale, 1.4426950408889634f);
     float m = -5000000.0f;
     for (int j = 0; j < T; ++j) {
@@ -243,10 +250,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(&bar->s_free[b]);
 
-      const float4 ksv = __ldg(reinterpret_cast<const float4*>(p.ks + bh * p.nks + j * 4));
+      float4 ksv;
+      if constexpr (QF8) {
+        const float kv = __ldg(p.ks + bh * p.nks + j / p.kq_tiles);
+        ksv = make_float4(kv, kv, kv, kv);
+      } else {
+        ksv = __ldg(reinterpret_cast<const float4*>(p.ks + bh * p.nks + j * 4));
+      }
       const float ksg[4] = {ksv.x, ksv.y, ksv.z, ksv.w};
-      const bool last = (j == T - 1);
-      const int valid = last ? static_cast<int>(p.Sk - int64_t(j) * 128) : 128;
+      const int valid = j == T - 1 ? static_cast<int>(p.Sk - int64_t(j) * 128) : 128;
+      // INT8: the reference's last-tile order (raw * qs * ks) * scale; E4M3 blocks: one order on every tile
+      const bool last = j == T - 1 && !QF8;
       // per-column-group logit multipliers (a group shares one K scale)
       float f1[4], f2[4];
 #pragma unroll
@@ -255,24 +269,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         f1[g] = last ? dq : __fmul_rn(scale, dq);   // first multiply
         f2[g] = scale;                              // second multiply (last tile only)
       }
+      auto rawf = [&](int c) -> float {
+        return QF8 ? __uint_as_float(raw[c]) : __int2float_rn(static_cast<int>(raw[c]));
+      };
       auto logit = [&](int c) -> float {
-        const float x = __int2float_rn(static_cast<int>(raw[c]));
+        const float x = rawf(c);
         const int g = (c >> 1) & 3;
         return last ? __fmul_rn(__fmul_rn(x, f1[g]), f2[g]) : __fmul_rn(x, f1[g]);
       };
       float alpha, mass = 0.f;
       uint32_t pw[32];
       if constexpr (EXPCAST) {
-        int gm[4] = {INT_MIN, INT_MIN, INT_MIN, INT_MIN};
-#pragma unroll
-        for (int c = 0; c < 128; ++c)
-          if (c < valid) gm[(c >> 1) & 3] = max(gm[(c >> 1) & 3], static_cast<int>(raw[c]));
         float lmax = -__int_as_float(0x7f800000);
+        if constexpr (QF8) {
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          if (gm[g] == INT_MIN) continue;
-          const float x = __int2float_rn(gm[g]);
-          lmax = fmaxf(lmax, last ? __fmul_rn(__fmul_rn(x, f1[g]), f2[g]) : __fmul_rn(x, f1[g]));
+          for (int c = 0; c < 128; ++c)
+            if (c < valid) lmax = fmaxf(lmax, logit(c));
+        } else {
+          int gm[4] = {INT_MIN, INT_MIN, INT_MIN, INT_MIN};
+#pragma unroll
+          for (int c = 0; c < 128; ++c)
+            if (c < valid) gm[(c >> 1) & 3] = max(gm[(c >> 1) & 3], static_cast<int>(raw[c]));
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            if (gm[g] == INT_MIN) continue;
+            const float x = __int2float_rn(gm[g]);
+            lmax = fmaxf(lmax, last ? __fmul_rn(__fmul_rn(x, f1[g]), f2[g]) : __fmul_rn(x, f1[g]));
+          }
         }
         const float mn = fmaxf(m, lmax);
         alpha = expf(m - mn);
@@ -296,16 +319,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           pw[w] = word;
         }
       } else {
-        // Sage FP8 probability (vc_reference.py:56-64): the row maximum is taken
-        // over fma(logit, 1, -8.807); P = e4m3(exp2(logit - m')), denominator
-        // uses the unrounded exp2 values.
-        const float off = 8.807f;
+        // FP8 probability control (vc_reference.py:56-64): the row maximum is
+        // taken over fma(logit, 1, -offset); P = e4m3(exp2(logit - m')), the
+        // denominator uses the unrounded exp2 values.  offset 8.807 is Sage's;
+        // 8 gives the Config contract's P8 = e4m3(256 exp(s - max)) with the
+        // exact exp row sums (src/vc_attention/core.py:357-360).
+        const float off = p.ctl_offset;
         float lmax = -__int_as_float(0x7f800000);
 #pragma unroll
         for (int c = 0; c < 128; ++c) {
           if (c >= valid) continue;
           const int g = (c >> 1) & 3;
-          const float x = __int2float_rn(static_cast<int>(raw[c]));
+          const float x = rawf(c);
           const float base = last ? __fmul_rn(x, f1[g]) : x;
           const float fac = last ? f2[g] : f1[g];
           lmax = fmaxf(lmax, __fmaf_rn(base, fac, -off));
@@ -322,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             pv[e] = 0.f;
             if (c < valid) {
               const int g = (c >> 1) & 3;
-              const float x = __int2float_rn(static_cast<int>(raw[c]));
+              const float x = rawf(c);
               const float base = last ? __fmul_rn(x, f1[g]) : x;
               const float fac = last ? f2[g] : f1[g];
               pv[e] = exp2f(__fmaf_rn(base, fac, -m));
@@ -475,10 +500,10 @@ bool make_map_3d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uin
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int D, typename OutT, bool EXPCAST, bool BV, bool VPB>
+template <int D, typename OutT, bool EXPCAST, bool BV, bool VPB, bool QF8 = false>
 int launch_attn(const AttnArgs& a, const CUtensorMap& mk, const CUtensorMap& mv, const Params& p, int64_t units,
                 cudaStream_t st) {
-  auto k = vc_attention_kernel<D, OutT, EXPCAST, BV, VPB>;
+  auto k = vc_attention_kernel<D, OutT, EXPCAST, BV, VPB, QF8>;
   const int smem = Smem<D>::kAlloc;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return VC_ERR_LAUNCH;
   k<<<static_cast<unsigned>(units), kThreads, smem, st>>>(mk, mv, p);
@@ -523,7 +548,15 @@ template <int D, typename OutT>
 int dispatch_flags(const AttnArgs& a, const Maps& m, const Params& p, int64_t units, int64_t pairs,
                    cudaStream_t st) {
   const bool alt = use_alt_kernel();
-  if (a.qk_e4m3) {   // E4M3 block Q/K: the tensor-memory kernels only (ExpCast, channel V scales)
+  if (a.qk_e4m3 && (!a.expcast || a.vs_per_block)) {
+    // E4M3 block Q/K with the FP8-P control or per-block V scales (the Config
+    // contract's own formats): the register-accumulating kernel
+    if (a.expcast) return launch_attn<D, OutT, true, true, true, true>(a, m.k, m.v, p, units, st);
+    if (!a.block_values) return launch_attn<D, OutT, false, false, false, true>(a, m.k, m.v, p, units, st);
+    if (a.vs_per_block) return launch_attn<D, OutT, false, true, true, true>(a, m.k, m.v, p, units, st);
+    return launch_attn<D, OutT, false, true, false, true>(a, m.k, m.v, p, units, st);
+  }
+  if (a.qk_e4m3) {   // E4M3 block Q/K, ExpCast, channel V scales: the tensor-memory kernels
     if (alt) {
       if (a.block_values) return launch_alt<D, OutT, true, true>(m, p, units, st);
       return launch_alt<D, OutT, false, true>(m, p, units, st);
@@ -611,6 +644,7 @@ int attention_fwd(const AttnArgs& a, cudaStream_t st) {
   p.pair_begin = pb;
   p.sm_scale = a.sm_scale;
   p.exact_expcast = a.expcast == 2 ? 1 : 0;
+  p.ctl_offset = a.config_control ? 8.0f : 8.807f;
   const int64_t units = ue - ub;
   // one CTA per SM: if the last wave of pairs would be at most half full, its
   // pairs run as two single-tile CTAs each (one wave of about half the length)

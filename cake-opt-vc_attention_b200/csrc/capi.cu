@@ -383,10 +383,15 @@ int vc_attention_fwd(const int8_t* q8, const float* qs, const int8_t* k8, const 
     set_last_error("%s: sm_scale must be positive and finite", fn);
     return VC_ERR_ARG;
   }
+  if (expcast < 0 || expcast > 3) {
+    set_last_error("%s: expcast must be 0 (FP8-P control), 1 (ExpCast), 2 (exact ExpCast) or 3 (FP8-P control, "
+                   "Config scaling)", fn);
+    return VC_ERR_ARG;
+  }
   if (int rc = check_device()) return rc;
   AttnArgs a{q8, qs, k8, ks, v8, vs, means, out, out_dtype, B, H, Sq, Sk, D, out_stride_b, out_stride_h, out_stride_s,
-             expcast == 2 ? 2 : (expcast ? 1 : 0), block_values ? 1 : 0, vs_per_block ? 1 : 0, sm_scale, unit_begin,
-             unit_end};
+             expcast == 3 ? 0 : expcast, block_values ? 1 : 0, vs_per_block ? 1 : 0, sm_scale, unit_begin,
+             unit_end, 0, 128, expcast == 3 ? 1 : 0};
   return finish(fn, attention_fwd(a, static_cast<cudaStream_t>(stream)));
 }
 
@@ -394,8 +399,8 @@ int vc_attention_fwd_e4m3qk(const uint8_t* q8, const float* qs, const uint8_t* k
                             const uint8_t* v8, const float* vs, const uint16_t* means, void* out, int out_dtype,
                             int64_t B, int64_t H, int64_t Sq, int64_t Sk, int64_t D, int64_t out_stride_b,
                             int64_t out_stride_h, int64_t out_stride_s, int expcast, int block_values,
-                            int64_t k_quant_block, float sm_scale, int64_t unit_begin, int64_t unit_end,
-                            void* stream) {
+                            int vs_per_block, int64_t k_quant_block, float sm_scale, int64_t unit_begin,
+                            int64_t unit_end, void* stream) {
   const char* fn = "vc_attention_fwd_e4m3qk";
   if (int rc = check_common(fn, VC_DTYPE_BF16, B, H, Sq, D)) return rc;
   if (int rc = check_common(fn, VC_DTYPE_BF16, B, H, Sk, D)) return rc;
@@ -409,9 +414,14 @@ int vc_attention_fwd_e4m3qk(const uint8_t* q8, const float* qs, const uint8_t* k
     return VC_ERR_ARG;
   }
   if (check_input(fn, "out", out, out_dtype, out_stride_b, out_stride_h, out_stride_s)) return VC_ERR_ARG;
-  if (expcast != 1 && expcast != 2) {
-    set_last_error("%s: the E4M3 Q/K kernel runs ExpCast only (expcast 1 or 2)", fn);
-    return VC_ERR_UNSUPPORTED;
+  if (expcast < 0 || expcast > 3) {
+    set_last_error("%s: expcast must be 0 (FP8-P control), 1 (ExpCast), 2 (exact ExpCast) or 3 (FP8-P control, "
+                   "Config scaling)", fn);
+    return VC_ERR_ARG;
+  }
+  if (vs_per_block && !block_values) {
+    set_last_error("%s: per-block V scales require block_values", fn);
+    return VC_ERR_ARG;
   }
   if (k_quant_block < 128 || k_quant_block % 128 || k_quant_block > 4096) {
     set_last_error("%s: k_quant_block must be a multiple of 128 in [128, 4096]", fn);
@@ -423,8 +433,9 @@ int vc_attention_fwd_e4m3qk(const uint8_t* q8, const float* qs, const uint8_t* k
   }
   if (int rc = check_device()) return rc;
   AttnArgs a{reinterpret_cast<const int8_t*>(q8), qs, reinterpret_cast<const int8_t*>(k8), ks, v8, vs, means, out,
-             out_dtype, B, H, Sq, Sk, D, out_stride_b, out_stride_h, out_stride_s, expcast, block_values ? 1 : 0, 0,
-             sm_scale, unit_begin, unit_end, 1, k_quant_block};
+             out_dtype, B, H, Sq, Sk, D, out_stride_b, out_stride_h, out_stride_s, expcast == 3 ? 0 : expcast,
+             block_values ? 1 : 0, vs_per_block ? 1 : 0, sm_scale, unit_begin, unit_end, 1, k_quant_block,
+             expcast == 3 ? 1 : 0};
   return finish(fn, attention_fwd(a, static_cast<cudaStream_t>(stream)));
 }
 

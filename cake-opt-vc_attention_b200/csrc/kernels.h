@@ -96,6 +96,7 @@ struct AttnArgs {
   int64_t unit_begin, unit_end;
   int qk_e4m3;        // 1: E4M3 block Q/K payloads (qs per 128-row Q tile, ks per kqb K rows)
   int64_t kqb;
+  int config_control; // FP8-P control with the Config contract's scaling (offset 8) instead of Sage's (8.807)
 };
 int attention_fwd(const AttnArgs& a, cudaStream_t st);
 // Copy (and optionally clear) the device error word of each kernel file on the

@@ -83,9 +83,6 @@ class Config:
                 raise ValueError("cuda_fp8 k_quant_block must be <= 4096")
         # sm100a: the fused kernel's fixed geometry
         if self.backend == "sm100a":
-            if self.qk_hadamard and not self.expcast:
-                raise ValueError("sm100a runs the Hadamard E4M3 Q/K path with ExpCast only; "
-                                 "set expcast=True, or qk_hadamard=False for the INT8 path")
             if self.qk_hadamard and (self.k_quant_block % 128 or self.k_quant_block > 4096):
                 raise ValueError("sm100a requires k_quant_block to be a multiple of 128, at most 4096")
             if self.q_block != 128 or self.kv_block != 128:

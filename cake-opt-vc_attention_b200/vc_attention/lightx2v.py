@@ -16,8 +16,8 @@ model.
 Built differently here: the call is parsed into an ``H3Call`` record, request
 bookkeeping lives in ``RequestTracker``, captures in ``CaptureSink``, and the
 registered layer (``H3VCAttention``) only composes them.  The arms run
-``Config(backend="sm100a")``; ``hadamard=True`` puts the ExpCast arms on the
-Config contract's own Hadamard E4M3 block Q/K path.  Capture mode returns
+``Config(backend="sm100a")``; ``hadamard=True`` puts the arms on the Config
+contract's own Hadamard E4M3 block Q/K path.  Capture mode returns
 torch's BF16 scaled-dot-product attention (the reference used MindIE on
 Ascend, which has no counterpart here).
 """
@@ -189,13 +189,12 @@ class CaptureSink:
 
 
 def arm_config(mode: str, *, hadamard: bool = False) -> Config:
-    """The sm100a Config of an experiment arm.  The Hadamard E4M3 block Q/K
-    path is taken only by arms with ExpCast (the INT8 Q/K path covers the
-    others)."""
+    """The sm100a Config of an experiment arm: INT8 Q/K, or with
+    ``hadamard`` the Config contract's Hadamard E4M3 block Q/K."""
     if mode not in ARMS:
         raise ValueError(f"unknown arm {mode!r}; arms are {sorted(ARMS)}")
     smooth, cast = ARMS[mode]
-    return Config(v_smooth=smooth, expcast=cast, backend="sm100a", qk_hadamard=bool(hadamard and cast))
+    return Config(v_smooth=smooth, expcast=cast, backend="sm100a", qk_hadamard=bool(hadamard))
 
 
 def sdpa_bf16(call: H3Call) -> torch.Tensor:
@@ -270,7 +269,7 @@ def configure(base: dict) -> dict:
 def parser() -> argparse.ArgumentParser:
     p = argparse.ArgumentParser(description="Run LightX2V with the sm100a VC attention layer (or capture Q/K/V)")
     p.add_argument("--mode", choices=MODES, required=True)
-    p.add_argument("--hadamard", action="store_true", help="ExpCast arms on the Hadamard E4M3 block Q/K path")
+    p.add_argument("--hadamard", action="store_true", help="the arms on the Hadamard E4M3 block Q/K path")
     p.add_argument("--output-dir", required=True)
     p.add_argument("--capture-steps", type=int, nargs="+", default=[0, 4])
     p.add_argument("--capture-layers", type=int, nargs="+", default=[0, 12])

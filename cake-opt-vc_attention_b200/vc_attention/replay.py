@@ -104,11 +104,10 @@ def metrics(actual: torch.Tensor, exact: torch.Tensor) -> dict:
 
 
 def arm_configs(*, clusters: int = 8, iterations: int = 2, hadamard: bool = False) -> dict:
-    """The sm100a Config of each arm.  ``hadamard`` moves the ExpCast arms to
-    the Hadamard E4M3 block Q/K path (the arms without ExpCast stay on INT8
-    Q/K)."""
+    """The sm100a Config of each arm: INT8 Q/K, or with ``hadamard`` the
+    Config contract's Hadamard E4M3 block Q/K."""
     return {name: Config(v_smooth=smooth, expcast=cast, backend="sm100a", clusters=clusters, iterations=iterations,
-                         qk_hadamard=bool(hadamard and cast))
+                         qk_hadamard=bool(hadamard))
             for name, (smooth, cast) in ARMS.items()}
 
 
@@ -168,7 +167,7 @@ def parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(description="Replay the four VC arms on one Q/K/V input (sm100a backend)")
     ap.add_argument("--capture", help="a capture .pt written by the LightX2V layer (else synthetic input)")
     ap.add_argument("--device", default="cuda:0")
-    ap.add_argument("--hadamard", action="store_true", help="ExpCast arms on the Hadamard E4M3 block Q/K path")
+    ap.add_argument("--hadamard", action="store_true", help="the arms on the Hadamard E4M3 block Q/K path")
     ap.add_argument("--tokens", type=int, default=1024)
     ap.add_argument("--heads", type=int, default=2)
     ap.add_argument("--dim", type=int, default=128)

@@ -1,9 +1,17 @@
 """sm100a backend of the Config API: the Hadamard E4M3 block Q/K path
-(``qk_hadamard=True``) or the INT8 ``sageattn_vc`` pipeline.
+(``qk_hadamard=True``) or the INT8 ``sageattn_vc`` Q/K path, with the
+Config contract's own V format and probabilities.
 
 Plays the role of the reference's cuda_backend.py:37-88 (``_attention``):
 validate the device, apply the request's V layout, prepare payloads and run
-the fused tcgen05 kernel, returning the reference's counter keys.
+a fused tcgen05 kernel, returning the reference's counter keys.  As in the
+contract (core.py:110-123, and the reference's native backend,
+csrc/kernels.cu:160-180), V is encoded per 128-token tile: the tile mean when
+smoothing is active (else zero), one scale per tile and channel; without
+ExpCast the probabilities are the FP8-P control P8 = e4m3(256 exp(s - max))
+with exact exp row sums (core.py:357-360).  Per-tile, per-channel V scales
+cannot be applied inside a tensor-memory accumulation, so this backend runs
+the register-accumulating kernel.
 """
 from __future__ import annotations
 
@@ -62,13 +70,11 @@ def attention(q, k, v, cfg, *, cache, step, total_steps, request_id, layer_id, s
         else:
             km = None if cfg.k_smooth else torch.zeros((B, H, 1, D), dtype=k.dtype, device=k.device)
             q8, qs, k8, ks, _ = ops.prep_qk_int8(q, k, perm=pi, km=km)
-        if active:
-            v8, vs, means = ops.prep_v_blocks(v, perm=pi, channel_scale=True)
-        else:
-            v8, vs = ops.prep_v_channel(v, perm=pi)
-            means = None
+        # per-tile V: residual over the tile mean (zero means when smoothing is off), per-tile scales
+        v8, vs, means = ops.prep_v_blocks(v, perm=pi, channel_scale=False, demean=active)
         out = ops.attention_fwd(q8, qs, k8, ks, v8, vs, means, out_dtype=q.dtype, sm_scale=float(scale),
-                                expcast=cfg.expcast, block_values=active, k_quant_block=cfg.k_quant_block)
+                                expcast=cfg.expcast, block_values=True, k_quant_block=cfg.k_quant_block,
+                                control="config")
     tiles = math.ceil(q.shape[-2] / 128) * math.ceil(k.shape[-2] / 128)
     return out, {
         "backend": "sm100a",

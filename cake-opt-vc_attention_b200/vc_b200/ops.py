@@ -212,19 +212,22 @@ def group_values(v: torch.Tensor, clusters: int = 8, iterations: int = 2, *, cen
 
 def attention_fwd(q8, qs, k8, ks, v8, vs, means, *, out_dtype=torch.bfloat16, sm_scale: float | None = None,
                   expcast: bool = True, block_values: bool = False, out: torch.Tensor | None = None,
-                  unit_range: tuple[int, int] | None = None, k_quant_block: int = 256) -> torch.Tensor:
+                  unit_range: tuple[int, int] | None = None, k_quant_block: int = 256,
+                  control: str = "sage") -> torch.Tensor:
     """Fused attention on prepared payloads.  Returns ``out`` [B,H,Sq,D].
 
     ``expcast``: True = ExpCast with the reference's folded affine encoder
     (its default H200 kernel), ``"exact"`` = the unfused decoded-payload
-    contract, False = Sage FP8 probabilities.
+    contract, False = the FP8-P control with ``control`` "sage" (Sage's
+    scaling, vc_reference.py:56-64) or "config" (the Config contract's
+    P8 = e4m3(256 exp(s - max)), core.py:357-360).
 
     ``unit_range`` = [begin, end) over units (b*H+h)*ceil(Sq/128)+q_tile
     computes only that shard (rows outside it are left untouched).
 
     Q/K payloads from ``prep_qk_hadamard`` (float8_e4m3fn) select the E4M3
-    block-QK kernel; ``k_quant_block`` is then their K scale block (ExpCast
-    and per-channel V scales only).
+    block-QK kernels; ``k_quant_block`` is then their K scale block.
+    Per-block V scales (``vs`` [B,H,T,D]) need ``block_values``.
     """
     _require_cuda("attention_fwd", q8, k8, v8)
     B, H, Sq, D = q8.shape
@@ -236,26 +239,28 @@ def attention_fwd(q8, qs, k8, ks, v8, vs, means, *, out_dtype=torch.bfloat16, sm
     scale = D ** -0.5 if sm_scale is None else float(sm_scale)
     if not (math.isfinite(scale) and scale > 0):
         raise ValueError("sm_scale must be positive and finite")
+    if vs.dim() == 4 and not block_values:
+        raise ValueError("per-block V scales need block_values=True")
+    if control not in ("sage", "config"):
+        raise ValueError("control must be 'sage' or 'config'")
     vs_per_block = bool(block_values and vs.dim() == 4)
+    mode = 2 if expcast == "exact" else 1 if expcast else (3 if control == "config" else 0)
     ub, ue = unit_range if unit_range is not None else (0, -1)
     lib = N.load()
     if q8.dtype == torch.float8_e4m3fn:
         if k8.dtype != torch.float8_e4m3fn:
             raise ValueError("E4M3 Q needs E4M3 K payloads")
-        if not expcast or vs_per_block:
-            raise ValueError("the E4M3 block-QK kernel runs ExpCast with per-channel V scales only")
         with torch.cuda.device(q8.device):
             N.check(lib.vc_attention_fwd_e4m3qk(_p(q8), _p(qs), _p(k8), _p(ks), _p(v8.view(torch.uint8)), _p(vs),
                                                 _p(means) if block_values else None, _p(out), _DT[out.dtype], B, H,
-                                                Sq, Sk, D, out.stride(0), out.stride(1), out.stride(2),
-                                                2 if expcast == "exact" else 1, int(block_values), int(k_quant_block),
-                                                scale, int(ub), int(ue), _stream(q8)), "vc_attention_fwd_e4m3qk")
+                                                Sq, Sk, D, out.stride(0), out.stride(1), out.stride(2), mode,
+                                                int(block_values), int(vs_per_block), int(k_quant_block), scale,
+                                                int(ub), int(ue), _stream(q8)), "vc_attention_fwd_e4m3qk")
         return out
     with torch.cuda.device(q8.device):
         N.check(lib.vc_attention_fwd(_p(q8), _p(qs), _p(k8), _p(ks), _p(v8.view(torch.uint8)), _p(vs),
                                      _p(means) if block_values else None, _p(out), _DT[out.dtype], B, H, Sq, Sk, D,
-                                     out.stride(0), out.stride(1), out.stride(2),
-                                     2 if expcast == "exact" else int(bool(expcast)), int(block_values),
+                                     out.stride(0), out.stride(1), out.stride(2), mode, int(block_values),
                                      int(vs_per_block), scale, int(ub), int(ue), _stream(q8)), "vc_attention_fwd")
     return out
 

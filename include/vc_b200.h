@@ -120,8 +120,11 @@ int vc_prep_v_channel(const void* v, int dtype, int64_t B, int64_t H, int64_t S,
  * 262144 (e.g. B*H <= 2048 at D = 128); larger sizes return VC_ERR_WORKSPACE
  * and launch nothing.  It allocates nothing: no cudaMalloc, no cudaFree.
  *   - The first call on each device (that device current) resolves the
- *     array's device address once (cudaGetSymbolAddress); make that first
- *     call before any stream capture on that device.
+ *     array's device address once (cudaGetSymbolAddress) and keeps it for the
+ *     life of the process; make that first call before any stream capture on
+ *     that device.  Resetting the device (cudaDeviceReset) or switching the
+ *     device's context after the first call is not supported: the kept
+ *     address would no longer be valid.
  *   - Every call on a device shares the one array.  Each call zeroes the
  *     words it uses on ``stream`` before its kernels read them, so calls in
  *     stream order are independent; calls that overlap on the GPU (other
@@ -165,10 +168,13 @@ int vc_group_values(const void* v, int dtype, int64_t B, int64_t H, int64_t S, i
  * (out_stride_b, out_stride_h, out_stride_s).  Work units are
  * (b*H + h) * ceil(Sq/128) + q_tile; [unit_begin, unit_end) selects a shard
  * (pass 0, -1 for all).  vs_per_block: vs is [B,H,T,D].  expcast: 0 = Sage
- * FP8 probabilities (control), 1 = ExpCast with the reference's folded affine
- * encoder (csrc/vc/vc_math.cuh:17-106, exact fallback on extreme ranges),
- * 2 = ExpCast with the unfused decoded-payload contract
- * (vc_reference.py:52-54).
+ * FP8 probabilities (control: P = e4m3(exp2(logit - max + 8.807)), exact
+ * exp2 row sums, vc_reference.py:56-64), 1 = ExpCast with the reference's
+ * folded affine encoder (csrc/vc/vc_math.cuh:17-106, exact fallback on
+ * extreme ranges), 2 = ExpCast with the unfused decoded-payload contract
+ * (vc_reference.py:52-54), 3 = the FP8-P control with the Config contract's
+ * scaling (P8 = e4m3(256 exp(s - max)), exact exp row sums;
+ * src/vc_attention/core.py:357-360).
  * Replaces _vc_sm90.forward (csrc/vc/vc_sm90.cu:1027-1123, vc_api.h:8-10). */
 int vc_attention_fwd(const int8_t* q8, const float* qs, const int8_t* k8, const float* ks, const uint8_t* v8,
                      const float* vs, const uint16_t* means, void* out, int out_dtype, int64_t B, int64_t H,
@@ -178,17 +184,20 @@ int vc_attention_fwd(const int8_t* q8, const float* qs, const int8_t* k8, const 
 
 /* vc_attention_fwd with E4M3 block Q/K payloads (vc_prep_qk_hadamard_e4m3):
  * QK^T is a tcgen05 kind::f8f6f4 MMA into FP32 and the logits are
- * raw * (sm_scale * (qs[q_tile] * ks[key / k_quant_block])).  ExpCast only
- * (expcast 1 or 2) with per-channel V scales (vs_per_block = 0); other
- * arguments as vc_attention_fwd.
+ * raw * (sm_scale * (qs[q_tile] * ks[key / k_quant_block])).  expcast
+ * 0-3, block_values and vs_per_block as vc_attention_fwd: ExpCast with
+ * per-channel V scales runs the tensor-memory-accumulating kernel; the FP8-P
+ * control and per-block V scales (the Config contract's own formats,
+ * core.py:110-123) run the register-accumulating kernel, since a per-tile,
+ * per-channel V scale cannot be applied inside a tensor-memory accumulation.
  * Replaces the cuda_fp8 backend's fused attention on its E4M3 block Q/K
  * (src/vc_attention/cuda_backend.py:37-88, core.py:335-345 semantics). */
 int vc_attention_fwd_e4m3qk(const uint8_t* q8, const float* qs, const uint8_t* k8, const float* ks,
                             const uint8_t* v8, const float* vs, const uint16_t* means, void* out, int out_dtype,
                             int64_t B, int64_t H, int64_t Sq, int64_t Sk, int64_t D, int64_t out_stride_b,
                             int64_t out_stride_h, int64_t out_stride_s, int expcast, int block_values,
-                            int64_t k_quant_block, float sm_scale, int64_t unit_begin, int64_t unit_end,
-                            void* stream);
+                            int vs_per_block, int64_t k_quant_block, float sm_scale, int64_t unit_begin,
+                            int64_t unit_end, void* stream);
 
 /* Failure-detection self-test (no counterpart in the reference, whose
  * kernels wait without bound, csrc/vc/vc_sm90.cu:114-128): one warp waits,

@@ -53,15 +53,20 @@ def main():
                     help="path of the reference checkout (or set VC_REFERENCE_ROOT)")
     ap.add_argument("--hadamard", action="store_true",
                     help="only (re)write the Hadamard / E4M3 block-QK fixtures (step 5)")
+    ap.add_argument("--config-defaults", action="store_true",
+                    help="only (re)write the Config-default fixtures (step 6)")
     args = ap.parse_args()
     if not args.reference:
         ap.error("give --reference <path-to-reference> or set VC_REFERENCE_ROOT")
     ref = Path(args.reference)
-    if args.hadamard:
+    if args.hadamard or args.config_defaults:
         sys.path.insert(0, str(ref / "src"))
         from vc_attention import core
         manifest = json.loads((HERE / "manifest.json").read_text())
-        hadamard_fixtures(core, manifest)
+        if args.hadamard:
+            hadamard_fixtures(core, manifest)
+        if args.config_defaults:
+            config_default_fixtures(core, manifest)
         (HERE / "manifest.json").write_text(json.dumps(manifest, indent=1, default=str) + "\n")
         return
     sage = ref / "third_party/sageattention_local/sageattention_local"
@@ -134,6 +139,7 @@ def main():
         manifest[name] = {"shape": list(shape), "config": kw, "counters": {k2: v2 for k2, v2 in counters.items()}}
 
     hadamard_fixtures(core, manifest)
+    config_default_fixtures(core, manifest)
     (HERE / "manifest.json").write_text(json.dumps(manifest, indent=1, default=str) + "\n")
     print(json.dumps(manifest, indent=1, default=str))
 
@@ -166,6 +172,24 @@ def hadamard_fixtures(core, manifest):
                                 dict(expcast=True, v_smooth=True, qk_hadamard=True, k_quant_block=128)),
     }
     for name, (seed, shape, dtype, koff, kw) in cfg_cases.items():
+        q, k, v = qk_inputs(seed, shape, dtype, koff)
+        out, counters = core.attention(q, k, v, core.Config(backend="reference", **kw))
+        np.savez_compressed(HERE / f"{name}.npz", seed=seed, shape=shape, koff=koff, out=out.numpy(),
+                            config=json.dumps(kw))
+        manifest[name] = {"shape": list(shape), "config": kw, "counters": {k2: v2 for k2, v2 in counters.items()}}
+
+
+def config_default_fixtures(core, manifest):
+    """6. The Config contract with the reference's defaults (no ExpCast: the
+    FP8-P control with exact exp row sums; Hadamard E4M3 block Q/K; V
+    encoded per 128-token tile) and its INT8-QK control: reference backend
+    outputs of core.attention."""
+    cases = {
+        "cfg_default": (25, (1, 2, 640, 128), torch.float32, 2 ** 0.5, {}),
+        "cfg_default_smooth": (26, (1, 2, 500, 64), torch.float32, 1.0, dict(v_smooth=True)),
+        "cfg_control_int8": (27, (1, 2, 384, 128), torch.float32, 2 ** 0.5, dict(qk_hadamard=False)),
+    }
+    for name, (seed, shape, dtype, koff, kw) in cases.items():
         q, k, v = qk_inputs(seed, shape, dtype, koff)
         out, counters = core.attention(q, k, v, core.Config(backend="reference", **kw))
         np.savez_compressed(HERE / f"{name}.npz", seed=seed, shape=shape, koff=koff, out=out.numpy(),

@@ -105,10 +105,12 @@ def test_e4m3_qk_entries_reject_bad_arguments_on_host(lib):
     assert lib.vc_prep_qk_hadamard_workspace_bytes(1, 2, 300, 300, 128, 100) < 0
     assert lib.vc_prep_qk_hadamard_workspace_bytes(1, 2, 300, 300, 128, 256) > 0
     args = [p] * 7 + [p, N.VC_DTYPE_BF16, 1, 2, 300, 300, 128, 2 * 300 * 128, 300 * 128, 128]
-    assert lib.vc_attention_fwd_e4m3qk(*args, 0, 0, 256, 0.125, 0, -1, None) == N.VC_ERR_UNSUPPORTED
-    assert "ExpCast" in _last(lib)
-    assert lib.vc_attention_fwd_e4m3qk(*args, 1, 0, 100, 0.125, 0, -1, None) == N.VC_ERR_ARG
-    assert lib.vc_attention_fwd_e4m3qk(*args, 1, 0, 256, -1.0, 0, -1, None) == N.VC_ERR_ARG
+    assert lib.vc_attention_fwd_e4m3qk(*args, 4, 0, 0, 256, 0.125, 0, -1, None) == N.VC_ERR_ARG
+    assert "expcast" in _last(lib)
+    assert lib.vc_attention_fwd_e4m3qk(*args, 1, 0, 1, 256, 0.125, 0, -1, None) == N.VC_ERR_ARG
+    assert "block_values" in _last(lib)
+    assert lib.vc_attention_fwd_e4m3qk(*args, 1, 0, 0, 100, 0.125, 0, -1, None) == N.VC_ERR_ARG
+    assert lib.vc_attention_fwd_e4m3qk(*args, 1, 0, 0, 256, -1.0, 0, -1, None) == N.VC_ERR_ARG
     assert "sm_scale" in _last(lib)
 
 

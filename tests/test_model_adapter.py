@@ -121,9 +121,10 @@ def test_layer_steps_layers_and_requests():
 def test_arm_configs():
     assert not X.arm_config("fp8_control").expcast and not X.arm_config("fp8_control").v_smooth
     assert X.arm_config("expcast", hadamard=True).qk_hadamard
-    assert not X.arm_config("v_smooth", hadamard=True).qk_hadamard   # no ExpCast: INT8 Q/K
+    assert X.arm_config("fp8_control", hadamard=True).qk_hadamard    # the Config contract's own control arm
+    assert not X.arm_config("v_smooth").qk_hadamard
     cfgs = R.arm_configs(hadamard=True)
-    assert set(cfgs) == set(R.ARMS) and cfgs["combined"].qk_hadamard and not cfgs["fp8_control"].qk_hadamard
+    assert set(cfgs) == set(R.ARMS) and all(c.qk_hadamard for c in cfgs.values())
     with pytest.raises(ValueError, match="unknown arm"):
         X.arm_config("capture")
 

@@ -35,7 +35,6 @@ def test_config_defaults_match_the_reference():
     ({"backend": "tpu"}, "backend"),
     ({"backend": "cuda_fp8", "quantize": False}, "quantize"),
     ({"backend": "cuda_fp8", "k_quant_block": 200}, "divide"),
-    ({"backend": "sm100a"}, "qk_hadamard=False"),
     ({"backend": "sm100a", "expcast": True, "k_quant_block": 200}, "multiple of 128"),
     ({"backend": "sm100a", "expcast": True, "k_quant_block": 8192}, "multiple of 128"),
     ({"backend": "sm100a", "qk_hadamard": False, "quantize": False}, "quantize"),
@@ -53,6 +52,9 @@ def test_sm100a_config_accepts_its_contract():
     c = Config(backend="sm100a", qk_hadamard=False, expcast=True, v_smooth=True)
     assert c.backend == "sm100a"
     assert Config(backend="sm100a", qk_hadamard=False, v_smooth=True, clusters=256).clusters == 256
+    # the reference's defaults (no ExpCast, Hadamard E4M3 block Q/K) are accepted
+    d = Config(backend="sm100a")
+    assert not d.expcast and d.qk_hadamard and d.k_quant_block == 256
 
 
 def _qkv(shape=(1, 2, 5, 64), dtype=torch.float16):

@@ -4,7 +4,10 @@ Its scratch is a library-owned static device array shared by every call, so
 the test makes two calls in a row whose inputs differ in shape and scale (a
 stale amax left by the first call would corrupt the second) and checks each
 against the workspace entry point vc_prep_v_channel, bit for bit (the
-tolerance every E4M3 V-payload test here uses).  Named to be collected last.
+tolerance every E4M3 V-payload test here uses).  Each call is checked to
+allocate nothing: neither torch's caching allocator nor the device's free
+memory (cudaMemGetInfo) moves across it.  The array is also filled exactly to
+its limit once.  Named to be collected last.
 """
 import ctypes as C
 
@@ -25,14 +28,20 @@ def _static_call(v, perm=None):
     npad = (S + 127) // 128 * 128
     v8 = torch.empty((B, H, D, npad), dtype=torch.uint8, device=v.device)
     vs = torch.empty((B, H, D), dtype=torch.float32, device=v.device)
-    stream = torch.cuda.current_stream(v.device).cuda_stream
-    before = torch.cuda.memory_allocated(v.device)
-    rc = lib.vc_prep_v_channel_static(C.c_void_p(v.data_ptr()), _DT[v.dtype], B, H, S, D, v.stride(0),
-                                      v.stride(1), v.stride(2),
-                                      C.c_void_p(perm.data_ptr() if perm is not None else 0),
-                                      C.c_void_p(v8.data_ptr()), C.c_void_p(vs.data_ptr()), C.c_void_p(stream))
-    N.check(rc, "vc_prep_v_channel_static")
-    assert torch.cuda.memory_allocated(v.device) == before
+    # the entry point works on the current device: make it the tensors' device
+    with torch.cuda.device(v.device):
+        stream = torch.cuda.current_stream(v.device).cuda_stream
+        torch.cuda.synchronize(v.device)
+        before = torch.cuda.memory_allocated(v.device)
+        free_before = torch.cuda.mem_get_info(v.device)[0]
+        rc = lib.vc_prep_v_channel_static(C.c_void_p(v.data_ptr()), _DT[v.dtype], B, H, S, D, v.stride(0),
+                                          v.stride(1), v.stride(2),
+                                          C.c_void_p(perm.data_ptr() if perm is not None else 0),
+                                          C.c_void_p(v8.data_ptr()), C.c_void_p(vs.data_ptr()), C.c_void_p(stream))
+        N.check(rc, "vc_prep_v_channel_static")
+        torch.cuda.synchronize(v.device)
+        assert torch.cuda.memory_allocated(v.device) == before
+        assert torch.cuda.mem_get_info(v.device)[0] == free_before, "device memory was allocated"
     return v8, vs
 
 
@@ -64,6 +73,17 @@ def test_static_scratch_matches_workspace_entry_two_calls(cuda_device):
         assert torch.equal(vs_s, vs_w), f"scales differ for {shape}"
         assert torch.equal(v8_s, v8_w.view(torch.uint8)), f"payload differs for {shape}"
         assert (vs_s[..., 3] == 0).all()
+    assert N.error_word(0) == 0
+
+
+def test_static_scratch_exactly_full(cuda_device):
+    """B*H*D = 262144 words: the whole array, its last word included."""
+    _static_call(_input(13, (1, 2, 200, 128), torch.bfloat16, 1.0, cuda_device))   # first call: address resolved
+    v = _input(14, (1, 2048, 16, 128), torch.bfloat16, 3.0, cuda_device)
+    v8_s, vs_s = _static_call(v)
+    v8_w, vs_w = ops.prep_v_channel(v)
+    torch.cuda.synchronize()
+    assert torch.equal(vs_s, vs_w) and torch.equal(v8_s, v8_w.view(torch.uint8))
     assert N.error_word(0) == 0
 
 
