@@ -52,7 +52,7 @@ CONFIGS = {
 METRIC = "TOPS (4*B*H*S^2*D per call) at BNSD [1,28,37741,128] D128, sageattn_vc ExpCast (prep + fused kernel)"
 # DRAM bytes (read + write) of one full config-2 launch of the paired-tile kernel, from ncu
 # (profiles/vc_attention_pair_kernel_c2_dram.txt)
-TRAFFIC_C2_BYTES = 530e6
+TRAFFIC_C2_BYTES = 647.7e6
 
 
 def peaks():
