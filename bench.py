@@ -397,8 +397,14 @@ def main():
     traffic = None
     if D == 128 and not smooth and S == 37741:
         traffic = TRAFFIC_C2_BYTES / 28 * nbh
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    plan = ops.attention_plan(sh.qtiles, local_shard.local_units, sms)
+    kernel = "vc_attention_pair_kernel"
+    if plan["tail_units"]:
+        kernel = (f"vc_attention_pair_kernel ({plan['pairs']} pairs) + vc_attention_alt_kernel "
+                  f"({plan['tail_units']} tail tiles), one event pair around both")
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_tops, "unit": "TFLOP/s",
-                "frac": achieved / peak_tops, "traffic": traffic, "kernel": "vc_attention_pair_kernel",
+                "frac": achieved / peak_tops, "traffic": traffic, "kernel": kernel,
                 "peak_basis": (f"min(measured dense INT8 {i8['tops']:.1f} TOPS [vc_tensor_peak: tcgen05 kind::i8, "
                                f"A in tensor memory, N=256, this run], 2 x bf16_tflops {2.0 * bf16:.1f} "
                                f"[{basis}, MEASURED_PEAKS.json])"),
@@ -481,8 +487,10 @@ def main():
     if rank == 0:
         # this library's kernels per step: K sums + mean finalize, Q/K tiles, then V channel amax +
         # quantise (no smoothing) or grouping (init, 2 assignments, update, histogram, scan, scatter)
-        # + block stats, channel scales, quantise; then the fused attention kernel
-        launches_per_step = (2 + 1 + 2 + 1) if not smooth else (2 + 1 + 7 + 3 + 1)
+        # + block stats, channel scales, quantise; then the fused attention kernel (the paired-tile
+        # kernel, plus the alternating-tile kernel for a short last wave)
+        launches_per_step = (2 + 1 + 2) if not smooth else (2 + 1 + 7 + 3)
+        launches_per_step += plan["launches"]
         line = {"metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "int8 QK / e4m3 PV (fp32 accumulate), bf16 I/O",

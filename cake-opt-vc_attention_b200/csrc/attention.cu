@@ -59,7 +59,6 @@ struct Params {
   int64_t kq_tiles;   // E4M3 block Q/K: K tiles per K scale
   int64_t unit_begin, unit_end;   // units (b*H+h)*qtiles + q_tile to compute
   int64_t pair_begin, qpairs;     // paired-tile kernel: first pair (b*H+h)*qpairs + q_tile/2, pairs per head
-  int64_t pair_solo_from;         // paired-tile kernel: CTAs from here on take single tiles of the remaining pairs
   float sm_scale;
   int exact_expcast;   // 1: unfused RN(RN(raw*f)-m) encoder instead of the folded affine one
   float ctl_offset;    // FP8-P control: P = e4m3(exp2(logit - max + offset)); 8.807 Sage, 8 the Config contract
@@ -511,8 +510,10 @@ int launch_attn(const AttnArgs& a, const CUtensorMap& mk, const CUtensorMap& mv,
 }
 
 // VC_B200_KERNEL selects another kernel for ExpCast + channel-scaled V:
-// "general" (register accumulation) or "alt" (one Q tile per CTA, the two
-// softmax groups alternating K tiles); the default is the paired-tile kernel.
+// "general" (register accumulation), "alt" (one Q tile per CTA, the two
+// softmax groups alternating K tiles) or "pair" (the paired-tile kernel for
+// every pair, no alternating-tile tail); the default is the paired-tile
+// kernel with the tail rule below.
 bool use_general_kernel() {
   const char* e = getenv("VC_B200_KERNEL");
   return e && strcmp(e, "general") == 0;
@@ -520,6 +521,10 @@ bool use_general_kernel() {
 bool use_alt_kernel() {
   const char* e = getenv("VC_B200_KERNEL");
   return e && strcmp(e, "alt") == 0;
+}
+bool use_pair_only() {
+  const char* e = getenv("VC_B200_KERNEL");
+  return e && strcmp(e, "pair") == 0;
 }
 
 struct Maps {
@@ -544,8 +549,26 @@ int launch_alt(const Maps& m, const Params& p, int64_t units, cudaStream_t st) {
   return cudaGetLastError() == cudaSuccess ? VC_OK : VC_ERR_LAUNCH;
 }
 
+// How a unit range is spread over the two tensor-memory kernels: the paired
+// kernel over `pairs` pairs from p.pair_begin, then the alternating-tile kernel
+// over tail.unit_begin .. tail.unit_end (tail_units of them, possibly none).
+struct Split {
+  int64_t pairs = 0;
+  Params tail;
+  int64_t tail_units = 0;
+};
+
+template <int D, typename OutT, bool BV, bool QF8 = false>
+int launch_split(const Maps& m, const Params& p, const Split& sp, cudaStream_t st) {
+  if (sp.pairs > 0) {
+    const int rc = launch_pair<D, OutT, BV, QF8>(m, p, sp.pairs, st);
+    if (rc != VC_OK) return rc;
+  }
+  return sp.tail_units > 0 ? launch_alt<D, OutT, BV, QF8>(m, sp.tail, sp.tail_units, st) : VC_OK;
+}
+
 template <int D, typename OutT>
-int dispatch_flags(const AttnArgs& a, const Maps& m, const Params& p, int64_t units, int64_t pairs,
+int dispatch_flags(const AttnArgs& a, const Maps& m, const Params& p, int64_t units, const Split& sp,
                    cudaStream_t st) {
   const bool alt = use_alt_kernel();
   if (a.qk_e4m3 && (!a.expcast || a.vs_per_block)) {
@@ -561,12 +584,12 @@ int dispatch_flags(const AttnArgs& a, const Maps& m, const Params& p, int64_t un
       if (a.block_values) return launch_alt<D, OutT, true, true>(m, p, units, st);
       return launch_alt<D, OutT, false, true>(m, p, units, st);
     }
-    if (a.block_values) return launch_pair<D, OutT, true, true>(m, p, pairs, st);
-    return launch_pair<D, OutT, false, true>(m, p, pairs, st);
+    if (a.block_values) return launch_split<D, OutT, true, true>(m, p, sp, st);
+    return launch_split<D, OutT, false, true>(m, p, sp, st);
   }
   if (a.expcast && !a.vs_per_block && !use_general_kernel() && !alt) {
-    if (a.block_values) return launch_pair<D, OutT, true>(m, p, pairs, st);
-    return launch_pair<D, OutT, false>(m, p, pairs, st);
+    if (a.block_values) return launch_split<D, OutT, true>(m, p, sp, st);
+    return launch_split<D, OutT, false>(m, p, sp, st);
   }
   if (a.expcast && !a.vs_per_block && alt) {
     if (a.block_values) return launch_alt<D, OutT, true>(m, p, units, st);
@@ -646,19 +669,30 @@ int attention_fwd(const AttnArgs& a, cudaStream_t st) {
   p.exact_expcast = a.expcast == 2 ? 1 : 0;
   p.ctl_offset = a.config_control ? 8.0f : 8.807f;
   const int64_t units = ue - ub;
-  // one CTA per SM: if the last wave of pairs would be at most half full, its
-  // pairs run as two single-tile CTAs each (one wave of about half the length)
+  // One CTA per SM.  If the last wave of pairs would be at most half full, the
+  // tiles of those pairs (at most one per SM) run on the alternating-tile
+  // kernel after the full waves: about 0.6 of a pair period instead of one.
+  // The tail pairs are the last ones of the range, so their units are the
+  // range's last ones too.
   const int64_t npairs = pe - pb, sms = sm_count(), tail = npairs % sms;
-  p.pair_solo_from = tail <= sms / 2 ? npairs - tail : npairs;
-  const int64_t pairs = npairs + (npairs - p.pair_solo_from);   // CTAs of the paired-tile kernel
+  Split sp;
+  sp.pairs = npairs;
+  if (!use_pair_only() && tail > 0 && tail <= sms / 2) {
+    const int64_t first = pe - tail;   // the first tail pair
+    const int64_t ut = (first / p.qpairs) * qtiles + (first % p.qpairs) * 2;
+    sp.pairs = npairs - tail;
+    sp.tail = p;
+    sp.tail.unit_begin = ut > ub ? ut : ub;
+    sp.tail_units = ue - sp.tail.unit_begin;
+  }
   if (a.out_dtype == VC_DTYPE_BF16)
-    return a.D == 128 ? dispatch_flags<128, __nv_bfloat16>(a, m, p, units, pairs, st)
-                      : dispatch_flags<64, __nv_bfloat16>(a, m, p, units, pairs, st);
+    return a.D == 128 ? dispatch_flags<128, __nv_bfloat16>(a, m, p, units, sp, st)
+                      : dispatch_flags<64, __nv_bfloat16>(a, m, p, units, sp, st);
   if (a.out_dtype == VC_DTYPE_F32)
-    return a.D == 128 ? dispatch_flags<128, float>(a, m, p, units, pairs, st)
-                      : dispatch_flags<64, float>(a, m, p, units, pairs, st);
-  return a.D == 128 ? dispatch_flags<128, __half>(a, m, p, units, pairs, st)
-                    : dispatch_flags<64, __half>(a, m, p, units, pairs, st);
+    return a.D == 128 ? dispatch_flags<128, float>(a, m, p, units, sp, st)
+                      : dispatch_flags<64, float>(a, m, p, units, sp, st);
+  return a.D == 128 ? dispatch_flags<128, __half>(a, m, p, units, sp, st)
+                    : dispatch_flags<64, __half>(a, m, p, units, sp, st);
 }
 
 cudaError_t attention_error_word(uint32_t* code, bool clear) { return read_tu_error_word(code, clear); }

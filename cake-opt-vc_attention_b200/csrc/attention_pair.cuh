@@ -32,16 +32,17 @@
 // tensor memory), so s32 scores read back as the floats 1.5*2^23 + s.
 //
 // Tensor memory (512 columns):
-//   D = 128: S [0,128) one score slot, used in the order A(0), B(0), A(1), ...
-//            O_A [128,272)  O_B [288,432)  preset A operand [432,440)
+//   S [0,128): one score slot, used in the order A(0), B(0), A(1), ...
+//   D = 128: O_A [128,272)  O_B [288,432)  preset A operand [432,440)
 //            P_A [448,480)  P_B [480,512);  Q_A, Q_B in shared memory
-//   D = 64:  S_A [0,128) S_B [128,256)   one slot per tile
-//            O_A [256,336)  O_B [336,416)  Q_A [416,432)  Q_B [432,448)
+//   D = 64:  O_A [256,336)  O_B [336,416)  Q_A [416,432)  Q_B [432,448)
 //            P_A [448,480)  P_B [480,512)
-// At D = 128 a second score slot does not fit, so QK^T issue n = 2j + X uses
-// slot n % NS and may overwrite it once the scores of issue n - NS have been
-// read; that round trip (issuer wake-up, preset and QK^T MMAs, group
-// wake-up, score read) bounds the tile period there.
+// QK^T issue n = 2j + X overwrites the slot once the scores of issue n - 1
+// (the other chain's) have been read, so the two groups alternate.  At
+// D = 128 a second slot does not fit; at D = 64 it does, but two slots let
+// the groups run in phase (both computing, then both waiting) and measured
+// 8% slower.  The round trip (issuer wake-up, preset and QK^T MMAs, group
+// wake-up, score read) bounds the tile period.
 // O_X holds D FP32 output columns plus a 16-column block whose first column
 // accumulates P.1 (the ExpCast denominator) through a row of E4M3 1.0
 // appended to every V tile.
@@ -60,11 +61,11 @@
 // PV_X(8k+8)); the P.V issuer issues its MMA right after PV_X(8k+8) and
 // commits pv_done_X after it, so the next rescale of O follows it.
 //
-// Tail balance.  When the last wave of pair CTAs would be at most half full,
-// the host splits those last pairs into single-tile ("solo") CTAs: tile A only,
-// one chain, one score slot (issue j waits for the read of tile j-1, so no
-// wait can alias a phase two ahead), group B idle.  The tail then costs about
-// one single-tile period instead of a full pair period.
+// Tail balance.  A CTA with one tile would cost about as much as a pair (one
+// group's softmax work per tile sets its period), so when the last wave of
+// pairs would be at most half full the host runs those pairs' tiles on the
+// alternating-tile kernel instead (both groups on one tile, about 0.6 of a
+// pair period) and launches this kernel on the full waves only.
 //
 // Barrier phases.  Every wait is unconditional and taken once per phase in
 // order, and no barrier can complete a phase ahead of its waiter: s_full_X,
@@ -79,10 +80,9 @@ constexpr int kPVS = 3;   // V ring depth
 
 template <int D>
 struct PairCols {
-  static constexpr int kNS = D == 64 ? 2 : 1;                 // score slots
   static constexpr bool kQTmem = D == 64;                     // Q in tensor memory (else shared, by TMA)
   static constexpr bool kPresetTmem = D == 128;               // preset A operand in tensor memory
-  static constexpr uint32_t kS = 0;                           // slot s at kS + 128 s
+  static constexpr uint32_t kS = 0;                           // the score slot
   static constexpr uint32_t kOA = D == 64 ? 256 : 128;
   static constexpr uint32_t kOB = D == 64 ? 336 : 288;
   static constexpr uint32_t kQA = 416, kQB = 432;             // D = 64 only
@@ -150,14 +150,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffSlot);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // CTAs [0, pair_solo_from) take pairs pair_begin + i; after them each pair
-  // is split into two solo CTAs (tile A = the pair's first, then second tile)
-  const bool solo = static_cast<int64_t>(blockIdx.x) >= p.pair_solo_from;
-  const int64_t k_solo = static_cast<int64_t>(blockIdx.x) - p.pair_solo_from;
-  const int64_t pair = p.pair_begin + (solo ? p.pair_solo_from + (k_solo >> 1) : static_cast<int64_t>(blockIdx.x));
+  const int64_t pair = p.pair_begin + static_cast<int64_t>(blockIdx.x);
   const int64_t bh = pair / p.qpairs;
-  const int64_t qt0 = (pair - bh * p.qpairs) * 2 + (solo ? (k_solo & 1) : 0);   // tile A; tile B = qt0 + 1
-  const int nchain = solo ? 1 : 2;
+  const int64_t qt0 = (pair - bh * p.qpairs) * 2;   // tile A; tile B = qt0 + 1
   const int T = static_cast<int>(p.ktiles);
 
   if (threadIdx.x == 0) {
@@ -278,7 +273,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       }
     } else if (warp == 9) {
       // ------------------------------------------------------- QK^T issuer
-      // issue n = 2j + X into slot n % NS once the scores of issue n - NS are read
+      // issue n = 2j + X into the slot once the scores of issue n - 1 are read
       constexpr uint32_t idesc_qk = QF8 ? idesc_make(1, 0, 0, 128, 128) : idesc_make(2, 1, 1, 128, 128);
       constexpr uint32_t idesc_preset = idesc_make(1, 0, 0, 128, 128);   // f32 <- f16 x f16
       const uint64_t adesc_preset = smem_desc_plain(smem_u32(smem + L::kOffPresetA), 128, 256);
@@ -292,18 +287,17 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const int s = j % kPKS;
         if (!mbar_wait_warp(&bar->k_full[s], (j / kPKS) & 1, kErrTimeoutMma)) break;
         const uint64_t kd = kdesc0 + s * kStep;
-        for (int x = 0; x < nchain; ++x) {
-          // pair: issue n = 2j + x into slot n % NS after the read of issue n - NS;
-          // solo: issue j into slot 0 after the read of tile j - 1
-          const int n = solo ? j : 2 * j + x, prev = n - (solo ? 1 : C::kNS);
-          const bool waited = prev < 0 || (solo ? mbar_wait_warp(&bar->s_free[0], prev & 1, kErrTimeoutMma)
-                                                : mbar_wait_warp(&bar->s_free[prev & 1], (prev >> 1) & 1, kErrTimeoutMma));
+        for (int x = 0; x < 2; ++x) {
+          // issue n = 2j + x after the read of issue n - 1 (chain prev & 1, its
+          // (prev >> 1)-th read)
+          const int prev = 2 * j + x - 1;
+          const bool waited = prev < 0 || mbar_wait_warp(&bar->s_free[prev & 1], (prev >> 1) & 1, kErrTimeoutMma);
           if (!waited) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t scol = tmem + C::kS + (solo ? 0u : 128u * (n % C::kNS));
+          const uint32_t scol = tmem + C::kS;
           const uint32_t qcol = tmem + (x ? C::kQB : C::kQA);
           const uint64_t qd = qdesc0 + x * kStep;
           if (elect_one()) {
@@ -346,7 +340,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const int s = j % kPVS;
         if (!mbar_wait_warp(&bar->v_full[s], (j / kPVS) & 1, kErrTimeoutMma)) break;
         const uint64_t vd = vdesc0 + s * kStepV;
-        for (int x = 0; x < nchain; ++x) {
+        for (int x = 0; x < 2; ++x) {
           if (!mbar_wait_warp(&bar->p_full[x], j & 1, kErrTimeoutMma)) {
             ok = false;
             break;
@@ -380,7 +374,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         if (elect_one()) mma_commit(&bar->v_empty[s]);
         __syncwarp();
       }
-      for (int x = 0; x < nchain; ++x) {
+      for (int x = 0; x < 2; ++x) {
         if constexpr (BV) {
           // the open batch of tile X, written by its group after the loop
           const int kb = (T - 1) >> 3;
@@ -410,7 +404,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const bool row_valid = row < p.Sq;   // (row < Sq implies qt < qtiles)
     const int64_t unit = bh * p.qtiles + qt;
     const bool write_row = row_valid && unit >= p.unit_begin && unit < p.unit_end;
-    const uint32_t scol = tmem + lane_base + C::kS + 128 * (C::kNS == 2 ? x : 0);
+    const uint32_t scol = tmem + lane_base + C::kS;
     const uint32_t ocol = tmem + lane_base + (x ? C::kOB : C::kOA);
     {
       if constexpr (C::kQTmem) {
@@ -456,7 +450,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
     for (int i = 0; i < 8; ++i) pend[i] = 0.f;
     uint8_t* massa = smem + L::kOffMassA + x * L::kMassA;
-    bool ok = x < nchain;   // group B of a solo CTA has no tile
+    bool ok = true;
     for (int j = 0; ok && j < T; ++j) {
       const float4 ksv = ksv_next;
       if (j + 1 < T) ksv_next = load_ks(j + 1);

@@ -265,6 +265,35 @@ def attention_fwd(q8, qs, k8, ks, v8, vs, means, *, out_dtype=torch.bfloat16, sm
     return out
 
 
+def attention_plan(qtiles: int, unit_range: tuple[int, int], sms: int) -> dict:
+    """How ``attention_fwd`` spreads a unit range over its ExpCast kernels
+    (channel-scaled V, the default kernel choice); the host rule in
+    csrc/attention.cu, restated for launch accounting.
+
+    Units [ub, ue) meet the pairs [pb, pe) (two consecutive Q tiles of one
+    head, ``ceil(qtiles/2)`` pairs per head).  One paired-tile CTA per SM: if
+    the last wave of pairs is at most half full (``0 < npairs % sms <= sms//2``)
+    those pairs' units run on the alternating-tile kernel after the full waves.
+    Returns ``{"pairs", "tail_units", "tail_begin", "launches"}``.
+    """
+    ub, ue = unit_range
+    if not 0 <= ub <= ue:
+        raise ValueError("unit_range must satisfy 0 <= begin <= end")
+    if ub == ue:
+        return {"pairs": 0, "tail_units": 0, "tail_begin": ue, "launches": 0}
+    qpairs = (qtiles + 1) // 2
+    pb = (ub // qtiles) * qpairs + (ub % qtiles) // 2
+    pe = ((ue - 1) // qtiles) * qpairs + ((ue - 1) % qtiles) // 2 + 1
+    npairs = pe - pb
+    tail = npairs % sms
+    if tail == 0 or tail > sms // 2:
+        return {"pairs": npairs, "tail_units": 0, "tail_begin": ue, "launches": 1}
+    first = pe - tail
+    ut = max(ub, (first // qpairs) * qtiles + (first % qpairs) * 2)
+    pairs = npairs - tail
+    return {"pairs": pairs, "tail_units": ue - ut, "tail_begin": ut, "launches": (pairs > 0) + 1}
+
+
 def kernel_resources(head_dim: int = 128) -> dict:
     import ctypes as C
     arr = (C.c_int64 * 4)()

@@ -35,15 +35,29 @@ class Shard:
         return self.unit_end - self.unit_begin
 
 
+def pair_unit(pair: int, qtiles: int) -> int:
+    """First unit of ``pair`` (pairs are two consecutive Q tiles of one head,
+    ``ceil(qtiles/2)`` per head; a head with an odd tile count ends in a
+    one-tile pair)."""
+    qpairs = (qtiles + 1) // 2
+    bh, i = divmod(pair, qpairs)
+    return bh * qtiles + 2 * i
+
+
 def shard(B: int, H: int, Sq: int, world: int, rank: int) -> Shard:
-    """Balanced contiguous split of the unit space (sizes differ by <= 1)."""
+    """Balanced contiguous split of the pair space (pair counts differ by
+    <= 1), as a unit range.  The attention kernel runs one pair of Q tiles
+    per CTA; cutting shards between pairs, never inside one, keeps every
+    rank's pair count at its share (config 2 on 8 GPUs: 518 pairs each, where
+    an even split of units gives some ranks 519)."""
     if not 0 <= rank < world:
         raise ValueError("rank out of range")
     qtiles = (Sq + 127) // 128
-    total = B * H * qtiles
+    total = B * H * ((qtiles + 1) // 2)
     base, extra = divmod(total, world)
-    ub = rank * base + min(rank, extra)
-    ue = ub + base + (1 if rank < extra else 0)
+    pb = rank * base + min(rank, extra)
+    pe = pb + base + (1 if rank < extra else 0)
+    ub, ue = pair_unit(pb, qtiles), pair_unit(pe, qtiles)
     if ue > ub:
         bh0, bh1 = ub // qtiles, (ue - 1) // qtiles + 1
     else:

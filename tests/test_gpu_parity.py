@@ -690,6 +690,10 @@ PAIR_CASES = [
     ((1, 1, 300, 64), 1300, True),
     ((1, 2, 1000, 128), 1000, True),
     ((2, 1, 129, 128), 2100, True),
+    # 150 pairs: one full wave of pairs on 148 SMs, then 4 tail tiles on the
+    # alternating-tile kernel (and other splits for the unit-range cuts)
+    ((1, 2, 19200, 128), 300, False),
+    ((1, 2, 19100, 64), 260, True),
 ]
 
 
@@ -699,7 +703,8 @@ def test_paired_tile_kernel_equals_alternating_kernel(ops, monkeypatch, shape, s
     performs every row's arithmetic in the same order as the alternating-tile
     kernel (one Q tile per CTA, the groups alternating K tiles), so the two
     give identical bits: INT8 and E4M3 Q/K, with and without block means, and
-    as unit ranges that cut pairs in two."""
+    as unit ranges that cut pairs in two.  The default schedule (full waves of
+    pairs, a short last wave on the alternating-tile kernel) equals both."""
     B, H, Sq, D = shape
     g = torch.Generator().manual_seed(51)
     q = torch.randn(B, H, Sq, D, generator=g).to(torch.bfloat16)
@@ -722,16 +727,24 @@ def test_paired_tile_kernel_equals_alternating_kernel(ops, monkeypatch, shape, s
         kw = dict(out_dtype=torch.float32, block_values=smooth)
         if scale is not None:
             kw["sm_scale"] = scale
-        pair = ops.attention_fwd(q8, qs, k8, ks, v8, vs, means, **kw)
-        split = torch.full_like(pair, float("nan"))
+        default = ops.attention_fwd(q8, qs, k8, ks, v8, vs, means, **kw)
         cuts = sorted({0, min(1, B * H * qtiles), B * H * qtiles // 2 + 1, B * H * qtiles})
-        for b, e in zip(cuts[:-1], cuts[1:]):
-            ops.attention_fwd(q8, qs, k8, ks, v8, vs, means, out=split, unit_range=(b, e), **kw)
+        outs = {}
+        for kernel in ("pair", "default"):
+            if kernel == "pair":
+                monkeypatch.setenv("VC_B200_KERNEL", "pair")
+            split = torch.full_like(default, float("nan"))
+            for b, e in zip(cuts[:-1], cuts[1:]):
+                ops.attention_fwd(q8, qs, k8, ks, v8, vs, means, out=split, unit_range=(b, e), **kw)
+            outs[kernel] = (ops.attention_fwd(q8, qs, k8, ks, v8, vs, means, **kw), split)
+            monkeypatch.delenv("VC_B200_KERNEL", raising=False)
         monkeypatch.setenv("VC_B200_KERNEL", "alt")
         alt = ops.attention_fwd(q8, qs, k8, ks, v8, vs, means, **kw)
         monkeypatch.delenv("VC_B200_KERNEL")
-        assert torch.equal(pair, alt)
-        assert torch.equal(split, pair)
+        assert torch.equal(outs["pair"][0], alt)
+        assert torch.equal(default, alt)
+        for whole, split in outs.values():
+            assert torch.equal(split, whole)
     assert ops.error_word(0, clear=True) == 0
 
 

@@ -222,10 +222,59 @@ def test_shards_cover_units_and_rows_exactly_once(B, H, S, world):
             assert s.bh_begin == s.unit_begin // qtiles and s.bh_end == (s.unit_end - 1) // qtiles + 1
             lb, le = s.local_units
             assert 0 <= lb < le <= (s.bh_end - s.bh_begin) * qtiles
+            # cut between pairs: every range starts on a pair's first tile
+            assert s.unit_begin % qtiles % 2 == 0
         prev_u, prev_r = s.unit_end, re_
-        sizes.append(s.num_units)
+        # pairs met by the range
+        sizes.append(len({(u // qtiles, u % qtiles // 2) for u in range(s.unit_begin, s.unit_end)}))
     assert prev_u == total and prev_r == B * H * S
     assert max(sizes) - min(sizes) <= 1
+
+
+def _pair_units(pair, qtiles):
+    qpairs = (qtiles + 1) // 2
+    bh, i = divmod(pair, qpairs)
+    return [bh * qtiles + t for t in (2 * i, 2 * i + 1) if t < qtiles]
+
+
+@pytest.mark.parametrize("B,H,S", [(1, 28, 37741), (2, 40, 75600), (2, 24, 16384), (1, 2, 19200), (1, 1, 100),
+                                   (2, 3, 129)])
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_attention_plan_splits_each_shard_into_full_waves_and_a_short_tail(B, H, S, world):
+    """The paired-tile kernel takes whole waves of pairs (one CTA per SM) and
+    the alternating-tile kernel the units of a last wave that is at most half
+    full; together they cover the shard's units exactly once."""
+    from vc_b200 import ops, parallel as P
+    sms = 148
+    qtiles = (S + 127) // 128
+    for r in range(world):
+        s = P.shard(B, H, S, world, r)
+        ub, ue = s.unit_begin, s.unit_end
+        plan = ops.attention_plan(qtiles, (ub, ue), sms)
+        if ub == ue:
+            assert plan["launches"] == 0
+            continue
+        pb = (ub // qtiles) * ((qtiles + 1) // 2) + (ub % qtiles) // 2
+        paired = {u for i in range(plan["pairs"]) for u in _pair_units(pb + i, qtiles) if ub <= u < ue}
+        tail = set(range(plan["tail_begin"], ue))
+        assert not paired & tail and paired | tail == set(range(ub, ue))
+        assert plan["tail_units"] == len(tail) <= sms
+        if plan["tail_units"]:
+            assert plan["pairs"] % sms == 0
+        else:
+            assert plan["pairs"] % sms == 0 or plan["pairs"] % sms > sms // 2
+    # config 2 on 8 GPUs: 518 pairs per rank = 3 full waves + a tail of 74 pairs (at most 148 tiles)
+    p8 = [ops.attention_plan(295, (P.shard(1, 28, 37741, 8, r).unit_begin, P.shard(1, 28, 37741, 8, r).unit_end),
+                             sms) for r in range(8)]
+    assert all(p["pairs"] == 444 and p["launches"] == 2 and 147 <= p["tail_units"] <= 148 for p in p8)
+    # on 2 and 4 GPUs the pairs fill 14 and 7 waves exactly
+    for world, waves in ((2, 14), (4, 7)):
+        for r in range(world):
+            s = P.shard(1, 28, 37741, world, r)
+            assert ops.attention_plan(295, (s.unit_begin, s.unit_end), sms)["pairs"] == waves * sms
+    # config 2 on one GPU: 4144 pairs = 28 full waves, no tail
+    assert ops.attention_plan(295, (0, 28 * 295), sms) == {"pairs": 4144, "tail_units": 0, "tail_begin": 8260,
+                                                         "launches": 1}
 
 
 def _gather_worker(rank, world, port, B, H, S, D, q):
