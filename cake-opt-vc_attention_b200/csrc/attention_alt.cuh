@@ -449,7 +449,6 @@ __global__ void __launch_bounds__(kAltThreads, 1)
       const bool safe = !p.exact_expcast && fabsf(mn) <= 128.f && scale >= 1.1754943508222875e-38f &&
                         isfinite(gain[0]) && isfinite(gain[1]) && isfinite(gain[2]) && isfinite(gain[3]);
       if (__all_sync(0xffffffffu, safe)) {
-#pragma unroll
         uint64_t gain2[4];
 #pragma unroll
         for (int g = 0; g < 4; ++g) gain2[g] = pk2f(gain[g], gain[g]);
