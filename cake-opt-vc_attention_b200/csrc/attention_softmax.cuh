@@ -1,6 +1,7 @@
-// Register-level helpers of the fused attention kernels: packed f32x2
-// arithmetic, saturating FMA, 3-input max, register reallocation, and the
-// K-major shared-memory descriptor choice.  Included by attention.cu.
+// Register-level helpers of the fused attention kernels: byte packing,
+// 3-input max, register reallocation, and the K-major shared-memory
+// descriptor choice (packed f32x2 arithmetic is in common.cuh).  Included by
+// attention.cu.
 //
 // Per-score arithmetic of the ExpCast encoders (no conversion-unit work):
 //   float(raw) = as_float(raw + 0x4B400000) - 1.5*2^23    (exact, |raw| < 2^22)
@@ -8,30 +9,6 @@
 //   byte       = sat_u8(bits(u * 2^-149))                    (RNE on the denormal grid)
 #pragma once
 
-__device__ __forceinline__ uint64_t pk2(uint32_t lo, uint32_t hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "r"(lo), "r"(hi));
-  return r;
-}
-__device__ __forceinline__ uint64_t pk2f(float lo, float hi) { return pk2(__float_as_uint(lo), __float_as_uint(hi)); }
-__device__ __forceinline__ void up2(uint64_t v, uint32_t& lo, uint32_t& hi) {
-  asm("mov.b64 {%0,%1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-  return r;
-}
 // (c[15:0] << 16) | (sat_u8(a) << 8) | sat_u8(b), a and b read as s32.
 __device__ __forceinline__ uint32_t pack_u8x2(uint32_t a, uint32_t b, uint32_t c) {
   uint32_t d;

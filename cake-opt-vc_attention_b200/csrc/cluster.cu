@@ -147,12 +147,13 @@ __global__ void __launch_bounds__(128) grp_assign(const T* __restrict__ v, int64
     const int r = threadIdx.x;
     const int64_t row = tile * kRows + r;
     const uint8_t* xrow = xs + r * L::kRowBytes;
-    float nrm[4] = {0.f, 0.f, 0.f, 0.f};
-    float dot[kMaxC][4];
+    // partials l = 0, 1 and l = 2, 3 as packed FP32 pairs: every half is the
+    // same chain of .rn operations as the scalar arithmetic, in half the
+    // instructions
+    uint64_t nrm01 = 0, nrm23 = 0;
+    uint64_t dot01[kMaxC], dot23[kMaxC];
 #pragma unroll
-    for (int c = 0; c < kMaxC; ++c)
-#pragma unroll
-      for (int l = 0; l < 4; ++l) dot[c][l] = 0.f;
+    for (int c = 0; c < kMaxC; ++c) dot01[c] = dot23[c] = 0;
 #pragma unroll 2
     for (int k = 0; k < L::kChunks; ++k) {
       float x[L::kEl];
@@ -160,24 +161,31 @@ __global__ void __launch_bounds__(128) grp_assign(const T* __restrict__ v, int64
 #pragma unroll
       for (int q = 0; q < L::kEl / 4; ++q) {
         const int j = k * (L::kEl / 4) + q;   // channels 4j .. 4j+3
-#pragma unroll
-        for (int l = 0; l < 4; ++l) nrm[l] = __fadd_rn(nrm[l], __fmul_rn(x[4 * q + l], x[4 * q + l]));
+        const uint64_t x01 = pk2f(x[4 * q], x[4 * q + 1]), x23 = pk2f(x[4 * q + 2], x[4 * q + 3]);
+        nrm01 = f2_add(nrm01, f2_mul(x01, x01));
+        nrm23 = f2_add(nrm23, f2_mul(x23, x23));
 #pragma unroll
         for (int c = 0; c < kMaxC; ++c) {
-          const float4 cv = *reinterpret_cast<const float4*>(&cen[c][4 * j]);
-          dot[c][0] = __fmaf_rn(x[4 * q + 0], cv.x, dot[c][0]);
-          dot[c][1] = __fmaf_rn(x[4 * q + 1], cv.y, dot[c][1]);
-          dot[c][2] = __fmaf_rn(x[4 * q + 2], cv.z, dot[c][2]);
-          dot[c][3] = __fmaf_rn(x[4 * q + 3], cv.w, dot[c][3]);
+          const ulonglong2 cv = *reinterpret_cast<const ulonglong2*>(&cen[c][4 * j]);   // (c0, c1), (c2, c3)
+          dot01[c] = f2_fma(x01, cv.x, dot01[c]);
+          dot23[c] = f2_fma(x23, cv.y, dot23[c]);
         }
       }
     }
-    const float norm = __fadd_rn(__fadd_rn(nrm[0], nrm[1]), __fadd_rn(nrm[2], nrm[3]));
+    uint32_t n0, n1, n2, n3;
+    up2(nrm01, n0, n1);
+    up2(nrm23, n2, n3);
+    const float norm = __fadd_rn(__fadd_rn(__uint_as_float(n0), __uint_as_float(n1)),
+                                 __fadd_rn(__uint_as_float(n2), __uint_as_float(n3)));
     float best_d = __int_as_float(0x7f800000);
     int best = 0;
 #pragma unroll
     for (int c = 0; c < kMaxC; ++c) {
-      const float dc = __fadd_rn(__fadd_rn(dot[c][0], dot[c][1]), __fadd_rn(dot[c][2], dot[c][3]));
+      uint32_t d0, d1, d2, d3;
+      up2(dot01[c], d0, d1);
+      up2(dot23[c], d2, d3);
+      const float dc = __fadd_rn(__fadd_rn(__uint_as_float(d0), __uint_as_float(d1)),
+                                 __fadd_rn(__uint_as_float(d2), __uint_as_float(d3)));
       const float dist = __fsub_rn(__fadd_rn(norm, cnorm[c]), __fmul_rn(2.f, dc));
       if (c < count && dist < best_d) {
         best_d = dist;

@@ -254,6 +254,12 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t 
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
                : "memory");
 }
+// The mbarrier's current phase also waits for every cp.async this thread has
+// issued so far (pending count +1 now, one arrival when they complete: no net
+// change to the expected count).
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
@@ -480,6 +486,37 @@ __device__ __forceinline__ uint64_t smem_desc_plain(uint32_t saddr, uint32_t lbo
   return d;                                             // layout 0: no swizzle
 }
 
+// Packed FP32 pairs (sm_100 f32x2 arithmetic): each half is rounded on its
+// own, exactly as the scalar .rn instruction would round it.
+__device__ __forceinline__ uint64_t pk2(uint32_t lo, uint32_t hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+__device__ __forceinline__ uint64_t pk2f(float lo, float hi) { return pk2(__float_as_uint(lo), __float_as_uint(hi)); }
+__device__ __forceinline__ void up2(uint64_t v, uint32_t& lo, uint32_t& hi) {
+  asm("mov.b64 {%0,%1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
 // UMMA instruction descriptor: dense, K-major A and B, M=128.
 //   [4,6) D format (1=f32, 2=s32) | [7,10) A fmt | [10,13) B fmt
 //   [17,23) N>>3 | [24,29) M>>4

@@ -148,9 +148,11 @@ __device__ __forceinline__ void store_i8(int8_t* p, const int8_t (&v)[N]) {
 // Q and K quantisation tiles, one persistent kernel.
 //
 // A tile is 128 tokens of one (b,h): Q tiles first, then K tiles.  A producer
-// warp streams each tile into a shared-memory ring with untiled bulk copies:
-// one copy per tile when its rows are contiguous, else one per row (arbitrary
-// row strides and the K permutation gather).  Two groups of eight compute
+// warp streams each tile into a shared-memory ring: one untiled bulk copy per
+// tile when its rows are contiguous, else (arbitrary row strides, the K
+// permutation gather) 16-byte cp.async by all 32 lanes, whole rows per
+// instruction, tracked by the stage's mbarrier.  One bulk copy per gathered
+// row measured 2.6x slower than the contiguous tiles.  Two groups of eight compute
 // warps take alternate tiles, quantise from shared memory and write int8 rows
 // and scales with coalesced stores.
 //   Q tile: warp w owns the 16-row Sage block w; scale group g = rows g, g+8.
@@ -232,24 +234,40 @@ __global__ void __launch_bounds__(kTileThreads, 1) qk_tiles(QKTileParams p) {
         if (!contiguous && !isq && p.perm && r < rows) src[i] = __ldg(p.perm + bh * S + r0 + r);
       }
       if (n >= L::kStages && !mbar_wait(&empty[s], ((n / L::kStages) & 1) ^ 1, kErrTimeoutProducer)) break;
-      if (lane == 0) mbar_expect_tx(&full[s], static_cast<uint32_t>(rows * L::kRow));
-      __syncwarp();
-      uint8_t* dst = sm + s * L::kStage;
-      if (contiguous) {   // contiguous rows: one copy for the tile
-        if (lane == 0) bulk_load(dst, base + r0 * ss, static_cast<uint32_t>(rows * L::kRow), &full[s]);
-        continue;
-      }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int r = lane + 32 * i;
-        if (r >= rows) break;
-        int64_t sr = src[i];
-        if (sr < 0 || sr >= S) {
+        if (lane + 32 * i < rows && (src[i] < 0 || src[i] >= S)) {
           raise_error(kErrBadIndex);   // out-of-range permutation entry: read row 0 instead
-          sr = 0;
+          src[i] = 0;
         }
-        bulk_load(dst + r * L::kRow, base + sr * ss, L::kRow, &full[s]);
       }
+      uint8_t* dst = sm + s * L::kStage;
+      if (contiguous) {   // contiguous rows: one copy for the tile
+        if (lane == 0) {
+          mbar_expect_tx(&full[s], static_cast<uint32_t>(rows * L::kRow));
+          bulk_load(dst, base + r0 * ss, static_cast<uint32_t>(rows * L::kRow), &full[s]);
+        }
+        __syncwarp();
+        continue;
+      }
+      // gathered or strided rows: chunk k of the tile is 16-byte piece k % CPR
+      // of row k / CPR; a warp instruction covers RPI whole rows, all inside
+      // one 32-row block, whose source rows lane r & 31 holds in src[r >> 5]
+      constexpr int CPR = L::kRow / 16, RPI = 32 / CPR;
+      static_assert(CPR <= 32 && 32 % CPR == 0, "a row is a divisor of 32 sixteen-byte pieces");
+      const int c = lane % CPR;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+#pragma unroll 4
+        for (int it = 0; it < 32 / RPI; ++it) {
+          const int r = 32 * i + it * RPI + lane / CPR;
+          const int64_t sr = __shfl_sync(0xffffffffu, src[i], r & 31);
+          if (r < rows) cp_async16(dst + r * L::kRow + c * 16, reinterpret_cast<const uint8_t*>(base + sr * ss) + c * 16, 16u);
+        }
+      }
+      cp_async_mbar_arrive(&full[s]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[s]);   // the phase's one counted arrival, after every lane's
     }
     return;
   }
