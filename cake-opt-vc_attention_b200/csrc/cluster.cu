@@ -11,7 +11,9 @@
 //     row FP32 arithmetic; ties pick the lowest centre index;
 //   * stable order of tokens inside each cluster.
 // Unlike the reference (shared-memory atomics), the centre statistics here are
-// accumulated in a fixed order, so results are bitwise reproducible.
+// accumulated in a fixed order (16-bit inputs: a tensor-core product whose
+// accumulation order the hardware fixes; FP32 inputs: token order), so
+// results are bitwise reproducible.
 //
 // More than 8 effective centres (up to 256) take the wide path, the policy of
 // the reference's public entry for that range (csrc/vc/pybind.cpp:6-44, its
@@ -94,9 +96,39 @@ __device__ __forceinline__ void chunk_f32(const uint8_t* p, float (&x)[16 / size
   }
 }
 
+// One m16n8k16 tensor-core product with FP32 accumulation, A row-major and B
+// column-major (16-bit inputs).  Used for the grouping statistics: the sums
+// of a tile's rows per centre are onehot(labels)^T x tile, whose products
+// (x * 1 or x * 0) are exact; the accumulation order is the hardware's fixed
+// one, so the sums are deterministic.
+template <typename T>
+__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (std::is_same<T, __half>::value) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+// Four transposed 8x8 16-bit matrices from shared memory (lane l gives the
+// address of row l % 8 of matrix l / 8).
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
 // Assign each token of a 128-token tile to its nearest centre.  With STATS,
-// also write this tile's per-centre channel sums and counts, accumulated by
-// thread d over the tile's rows in token order.
+// also write this tile's per-centre channel sums and counts: for 16-bit
+// inputs as onehot(labels)^T x tile on the tensor core (warp w: channels
+// 32w.. of D = 128, 16w.. of D = 64), for FP32 inputs by thread d over the
+// tile's rows in token order.
 //
 // The tile is staged in its input type by cp.async (every copy in flight at
 // once).  Thread r owns token r: for every centre it keeps the four partial
@@ -195,7 +227,49 @@ __global__ void __launch_bounds__(128) grp_assign(const T* __restrict__ v, int64
     lab[r] = row < S ? best : -1;
     if (row < S) labels[bh * S + row] = best;
   }
-  if constexpr (STATS) {
+  if constexpr (STATS && sizeof(T) == 2) {
+    __syncthreads();
+    constexpr int kNB = D / 8 / 4;   // 8-channel blocks per warp
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const uint32_t one = std::is_same<T, __half>::value ? 0x3C00u : 0x3F80u;
+    float acc[kNB][4];
+#pragma unroll
+    for (int nb = 0; nb < kNB; ++nb)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[nb][i] = 0.f;
+    const uint32_t xs0 = smem_u32(xs);
+#pragma unroll 2
+    for (int kb = 0; kb < kRows / 16; ++kb) {
+      // A = onehot: row g (centre g) of rows kb*16 + {2t, 2t+1, 2t+8, 2t+9}; centres 8..15 are zero
+      const int r0 = kb * 16 + 2 * t;
+      uint32_t a[4];
+      a[0] = (lab[r0] == g ? one : 0u) | ((lab[r0 + 1] == g ? one : 0u) << 16);
+      a[2] = (lab[r0 + 8] == g ? one : 0u) | ((lab[r0 + 9] == g ? one : 0u) << 16);
+      a[1] = a[3] = 0u;
+#pragma unroll
+      for (int nb = 0; nb < kNB; nb += 2) {
+        // B = rows kb*16 .. +15 of channel blocks 8*(warp*kNB + nb) and the next
+        const int m = lane >> 3, k = (m & 1) * 8 + (lane & 7);
+        const int cb = warp * kNB + nb + (m >> 1);
+        uint32_t b[4];
+        ldmatrix_x4_trans(b, xs0 + (kb * 16 + k) * L::kRowBytes + cb * 16);
+        mma_16816<T>(acc[nb], a, b[0], b[1]);
+        mma_16816<T>(acc[nb + 1], a, b[2], b[3]);
+      }
+    }
+    if (g < count) {
+#pragma unroll
+      for (int nb = 0; nb < kNB; ++nb) {
+        const int ch = (warp * kNB + nb) * 8 + 2 * t;
+        *reinterpret_cast<float2*>(psum + ((bh * tiles + tile) * count + g) * D + ch) = make_float2(acc[nb][0], acc[nb][1]);
+      }
+    }
+    if (threadIdx.x < count) {
+      int n = 0;
+      for (int r = 0; r < kRows; ++r) n += lab[r] == static_cast<int>(threadIdx.x);
+      pcnt[(bh * tiles + tile) * count + threadIdx.x] = n;
+    }
+  } else if constexpr (STATS) {
     __syncthreads();
     // thread d sums channel d of each centre's rows in token order; the
     // label is the same for the whole warp, so the switch does not diverge
