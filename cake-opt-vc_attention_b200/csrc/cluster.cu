@@ -306,22 +306,41 @@ __global__ void __launch_bounds__(128) grp_assign(const T* __restrict__ v, int64
   }
 }
 
-// centre = (sum over tiles, in tile order) / count; empty centres unchanged.
+// centre = (sum over tiles) / count; empty centres unchanged.  8*D threads
+// per (centre, head): group g sums the g-th eighth of the tiles in tile order,
+// and thread d of group 0 combines the eight sums in a fixed tree, so the
+// order is deterministic while eight chains run at once.
+constexpr int kUpdateGroups = 8;
 template <int D>
-__global__ void grp_update(float* __restrict__ centers, const float* __restrict__ psum,
-                           const int32_t* __restrict__ pcnt, int count, int64_t tiles) {
+__global__ void __launch_bounds__(kUpdateGroups * D) grp_update(float* __restrict__ centers,
+                                                                 const float* __restrict__ psum,
+                                                                 const int32_t* __restrict__ pcnt, int count,
+                                                                 int64_t tiles) {
+  __shared__ float part[kUpdateGroups][D];
+  __shared__ int64_t npart[kUpdateGroups];
   const int c = blockIdx.x;
   const int64_t bh = blockIdx.y;
-  const int d = threadIdx.x;
-  if (d >= D) return;
+  const int d = threadIdx.x % D, g = threadIdx.x / D;
+  const int64_t chunk = (tiles + kUpdateGroups - 1) / kUpdateGroups;
+  const int64_t t0 = min64(tiles, g * chunk), t1 = min64(tiles, t0 + chunk);
   float s = 0.f;
   int64_t n = 0;
-  for (int64_t t = 0; t < tiles; ++t) {
+  for (int64_t t = t0; t < t1; ++t) {
     const int64_t idx = (bh * tiles + t) * count + c;
     s = __fadd_rn(s, psum[idx * D + d]);
     n += pcnt[idx];
   }
-  if (n) centers[(bh * count + c) * D + d] = __fdiv_rn(s, static_cast<float>(n));
+  part[g][d] = s;
+  if (d == 0) npart[g] = n;
+  __syncthreads();
+  if (g == 0) {
+    const float tot = __fadd_rn(__fadd_rn(__fadd_rn(part[0][d], part[1][d]), __fadd_rn(part[2][d], part[3][d])),
+                                __fadd_rn(__fadd_rn(part[4][d], part[5][d]), __fadd_rn(part[6][d], part[7][d])));
+    int64_t nt = 0;
+#pragma unroll
+    for (int i = 0; i < kUpdateGroups; ++i) nt += npart[i];
+    if (nt) centers[(bh * count + c) * D + d] = __fdiv_rn(tot, static_cast<float>(nt));
+  }
 }
 
 // Stable counting sort, step 1: label histogram per chunk of kChunk tokens.
@@ -524,7 +543,7 @@ int launch_group(const GroupArgs& a, cudaStream_t st) {
     if (it + 1 < a.iterations) {
       grp_assign<T, D, true><<<dim3(tiles, BH), 128, smem, st>>>(v, a.H, S, a.sb, a.sh, a.ss, count, centers, labels,
                                                               psum, pcnt, tiles);
-      grp_update<D><<<dim3(count, BH), D, 0, st>>>(centers, psum, pcnt, count, tiles);
+      grp_update<D><<<dim3(count, BH), kUpdateGroups * D, 0, st>>>(centers, psum, pcnt, count, tiles);
     } else {
       grp_assign<T, D, false><<<dim3(tiles, BH), 128, smem, st>>>(v, a.H, S, a.sb, a.sh, a.ss, count, centers, labels,
                                                                nullptr, nullptr, tiles);

@@ -131,14 +131,33 @@ __device__ __forceinline__ float block_sum(const uint8_t* sin, int d) {
   return s[0];
 }
 
-// Block statistics pass (channel-scale mode): mean and residual peak per
-// (bh, tile, d) into the workspace (csrc/vc/preprocess.cu:68-88).
+// max over the tile's first ``count`` rows of |x - mean| in channel d, as four
+// independent chains (a maximum is exact in any order).
+template <typename T, int D>
+__device__ __forceinline__ float residual_peak(const uint8_t* sin, int d, int count, float mean) {
+  using G = TileGeom<T, D>;
+  float pk[4] = {0.f, 0.f, 0.f, 0.f};
+  int r = 0;
+  for (; r + 4 <= count; r += 4) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) pk[u] = fmaxf(pk[u], fabsf(__fsub_rn(smem_elem<T>(sin, G::kPitch, r + u, d), mean)));
+  }
+  for (; r < count; ++r) pk[0] = fmaxf(pk[0], fabsf(__fsub_rn(smem_elem<T>(sin, G::kPitch, r, d), mean)));
+  return fmaxf(fmaxf(pk[0], pk[1]), fmaxf(pk[2], pk[3]));
+}
+
+// Block statistics pass (channel-scale mode): the mean per (bh, tile, d) into
+// the workspace, and the maxima over tiles of the residual peak and of |mean|
+// per (bh, d) (csrc/vc/preprocess.cu:68-88).  The maxima are combined across
+// CTAs by atomicMax on the FP32 bits (values >= 0, so the bit order is the
+// value order; a maximum does not depend on the order of its operands); NaN
+// operands are skipped, as fmaxf skips them.
 template <typename T, int D>
 __global__ void __launch_bounds__(kTileThreads) v_block_stats(const T* __restrict__ v, int64_t H, int64_t S,
                                                               int64_t sb, int64_t sh, int64_t ss,
                                                               const int64_t* __restrict__ perm,
-                                                              float* __restrict__ ws_mean, float* __restrict__ ws_peak,
-                                                              int64_t tiles) {
+                                                              float* __restrict__ ws_mean, uint32_t* __restrict__ peak_bits,
+                                                              uint32_t* __restrict__ mabs_bits, int64_t tiles) {
   using G = TileGeom<T, D>;
   extern __shared__ __align__(128) uint8_t smem[];
   const int64_t tile = blockIdx.x, bh = blockIdx.y;
@@ -147,26 +166,24 @@ __global__ void __launch_bounds__(kTileThreads) v_block_stats(const T* __restric
   const int count = static_cast<int>(min64(128, S - tile * 128));
   for (int d = threadIdx.x; d < D; d += kTileThreads) {
     const float mean = __fdiv_rn(block_sum<T, D>(smem, d), static_cast<float>(count));
-    float peak = 0.f;
-    for (int r = 0; r < count; ++r) peak = fmaxf(peak, fabsf(__fsub_rn(smem_elem<T>(smem, G::kPitch, r, d), mean)));
+    const float peak = residual_peak<T, D>(smem, d, count, mean);
     ws_mean[(bh * tiles + tile) * D + d] = mean;
-    ws_peak[(bh * tiles + tile) * D + d] = peak;
+    const float mabs = fabsf(mean);
+    if (peak == peak) atomicMax(peak_bits + bh * D + d, __float_as_uint(peak));
+    if (mabs == mabs) atomicMax(mabs_bits + bh * D + d, __float_as_uint(mabs));
   }
 }
 
 // Channel scale s = max(max_t peak/448 (1 if 0), max_t |mean|/65504)
-// (csrc/vc/preprocess.cu:90-106).
+// (csrc/vc/preprocess.cu:90-106), from the two maxima over tiles that
+// v_block_stats accumulated.
 template <int D>
-__global__ void v_channel_scales(const float* __restrict__ ws_mean, const float* __restrict__ ws_peak,
-                                 float* __restrict__ vs, int64_t tiles) {
+__global__ void v_channel_scales(const uint32_t* __restrict__ peak_bits, const uint32_t* __restrict__ mabs_bits,
+                                 float* __restrict__ vs) {
   const int64_t bh = blockIdx.x;
   const int d = threadIdx.x;
   if (d >= D) return;
-  float pk = 0.f, mp = 0.f;
-  for (int64_t t = 0; t < tiles; ++t) {
-    pk = fmaxf(pk, ws_peak[(bh * tiles + t) * D + d]);
-    mp = fmaxf(mp, fabsf(ws_mean[(bh * tiles + t) * D + d]));
-  }
+  const float pk = __uint_as_float(peak_bits[bh * D + d]), mp = __uint_as_float(mabs_bits[bh * D + d]);
   const float s = pk > 0.f ? __fdiv_rn(pk, 448.f) : 1.0f;
   vs[bh * D + d] = fmaxf(s, __fdiv_rn(mp, 65504.f));
 }
@@ -214,8 +231,7 @@ __global__ void __launch_bounds__(kTileThreads) v_tile_quant(const T* __restrict
   if constexpr (MODE == kResidualBlock) {
     for (int d = threadIdx.x; d < D; d += kTileThreads) {
       const float mean = demean ? __fdiv_rn(block_sum<T, D>(sin, d), static_cast<float>(count)) : 0.f;
-      float peak = 0.f;
-      for (int r = 0; r < count; ++r) peak = fmaxf(peak, fabsf(__fsub_rn(smem_elem<T>(sin, G::kPitch, r, d), mean)));
+      const float peak = residual_peak<T, D>(sin, d, count, mean);
       float s = peak > 0.f ? __fdiv_rn(peak, 448.f) : 1.0f;
       s = fmaxf(s, __fdiv_rn(fabsf(mean), 65504.f));
       s_mul[d] = s;
@@ -282,12 +298,14 @@ int launch_v_blocks(const PrepVArgs& a, cudaStream_t st) {
   __half* means = reinterpret_cast<__half*>(a.means);
   if (a.channel_scale && a.demean) {
     float* ws_mean = static_cast<float*>(a.workspace);
-    float* ws_peak = ws_mean + BH * tiles * D;
+    uint32_t* peak_bits = reinterpret_cast<uint32_t*>(ws_mean + BH * tiles * D);
+    uint32_t* mabs_bits = peak_bits + BH * D;
+    if (cudaMemsetAsync(peak_bits, 0, 2 * BH * D * 4, st) != cudaSuccess) return VC_ERR_LAUNCH;
     auto ks = v_block_stats<T, D>;
     cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
     ks<<<dim3(tiles, BH), kTileThreads, G::kSmem, st>>>(static_cast<const T*>(a.v), a.H, a.S, a.sb, a.sh, a.ss,
-                                                        a.perm, ws_mean, ws_peak, tiles);
-    v_channel_scales<D><<<BH, D, 0, st>>>(ws_mean, ws_peak, a.vs, tiles);
+                                                        a.perm, ws_mean, peak_bits, mabs_bits, tiles);
+    v_channel_scales<D><<<BH, D, 0, st>>>(peak_bits, mabs_bits, a.vs);
     auto kq = v_tile_quant<T, D, kResidualChannel>;
     cudaFuncSetAttribute(kq, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
     kq<<<dim3(tiles, BH), kTileThreads, G::kSmem, st>>>(static_cast<const T*>(a.v), a.H, a.S, a.sb, a.sh, a.ss,
@@ -306,7 +324,7 @@ int launch_v_blocks(const PrepVArgs& a, cudaStream_t st) {
 int64_t prep_v_channel_workspace(int64_t B, int64_t H, int64_t, int64_t D) { return B * H * D * 4 + 256; }
 
 int64_t prep_v_blocks_workspace(int64_t B, int64_t H, int64_t S, int64_t D) {
-  return 2 * B * H * ((S + 127) / 128) * D * 4 + 256;
+  return (B * H * ((S + 127) / 128) * D + 2 * B * H * D) * 4 + 256;   // tile means + two maxima per channel
 }
 
 #define VCB_DISPATCH_V(FN)                                                    \
