@@ -106,6 +106,30 @@ __device__ __forceinline__ int8_t sage_i8(float x, float scale, float rscale) {
   return static_cast<int8_t>((mag ^ s) - s);
 }
 
+// sage_i8 for two values at once: the three operations of the quotient and
+// the round-down add run as packed FP32 pairs, each half rounded exactly as
+// the scalar instruction rounds it (fma(q0, -scale, x) is fma(-q0, scale, x):
+// negating a factor is exact).  nscale2 = (-scale, -scale), rscale2 = (rscale, rscale).
+__device__ __forceinline__ uint64_t f2_add_rd(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rm.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ void sage_i8x2(float xa, float xb, uint64_t nscale2, uint64_t rscale2, int8_t& oa,
+                                          int8_t& ob) {
+  const uint64_t x2 = pk2f(xa, xb);
+  const uint64_t q0 = f2_mul(x2, rscale2);
+  const uint64_t q2 = f2_fma(f2_fma(q0, nscale2, x2), rscale2, q0);
+  uint32_t qa, qb;
+  up2(q2, qa, qb);
+  const float ua = __fadd_rn(fabsf(__uint_as_float(qa)), 0.5f), ub = __fadd_rn(fabsf(__uint_as_float(qb)), 0.5f);
+  uint32_t ma, mb;
+  up2(f2_add_rd(pk2f(ua, ub), pk2f(8388608.f, 8388608.f)), ma, mb);
+  const int sa = static_cast<int>(qa) >> 31, sb = static_cast<int>(qb) >> 31;
+  oa = static_cast<int8_t>((static_cast<int>(ma & 0xFFu) ^ sa) - sa);
+  ob = static_cast<int8_t>((static_cast<int>(mb & 0xFFu) ^ sb) - sb);
+}
+
 // Two values rounded to T (RN) and held packed; unpack is exact.
 template <typename T>
 struct Pair;
@@ -287,8 +311,11 @@ __global__ void __launch_bounds__(kTileThreads, 1) qk_tiles(QKTileParams p) {
     const int64_t S = isq ? p.Sq : p.Sk;
     const int rows = static_cast<int>(min64(128, S - r0));
     if (isq) {
-      // Sage Q block: rows 16w .. 16w+15 of the tile, scale groups g = rows {g, g+8}
-#pragma unroll 2
+      // Sage Q block: rows 16w .. 16w+15 of the tile, scale groups g = rows {g, g+8}.
+      // The eight group maxima first; then lane g & 7 computes group g's scale,
+      // so the warp runs one division and one reciprocal instead of eight
+      float am[8];
+#pragma unroll
       for (int g = 0; g < 8; ++g) {
         const int r = 16 * warp + g + 8 * hf;
         float x[E];
@@ -301,16 +328,33 @@ __global__ void __launch_bounds__(kTileThreads, 1) qk_tiles(QKTileParams p) {
         float amax = 0.f;
 #pragma unroll
         for (int i = 0; i < E; ++i) amax = fmaxf(amax, fabsf(x[i]));
-        amax = warp_max(amax);
-        const float scale = __fadd_rn(__fdiv_rn(amax, 127.f), 1e-7f);
-        const float rscale = __frcp_rn(scale);
+        am[g] = warp_max(amax);
+      }
+      float mine = am[0];
+#pragma unroll
+      for (int g = 1; g < 8; ++g) mine = (lane & 7) == g ? am[g] : mine;
+      const float my_scale = __fadd_rn(__fdiv_rn(mine, 127.f), 1e-7f);
+      const float my_rscale = __frcp_rn(my_scale);
+      // scales exist for the 16-row blocks of Sq padded to 64 rows (all-padding blocks get 1e-7)
+      const int64_t blk16 = (r0 >> 4) + warp;
+      if (lane < 8 && blk16 * 8 < p.nscale) p.qs[bh * p.nscale + blk16 * 8 + lane] = my_scale;
+#pragma unroll 2
+      for (int g = 0; g < 8; ++g) {
+        const int r = 16 * warp + g + 8 * hf;
+        const float scale = __shfl_sync(0xffffffffu, my_scale, g);
+        const float rscale = __shfl_sync(0xffffffffu, my_rscale, g);
+        const uint64_t nscale2 = pk2f(-scale, -scale), rscale2 = pk2f(rscale, rscale);
+        float x[E];
+        if (r < rows) {
+          load_vec_smem<T, E>(tile + r * D + col, x);
+        } else {
+#pragma unroll
+          for (int i = 0; i < E; ++i) x[i] = 0.f;
+        }
         int8_t o[E];
 #pragma unroll
-        for (int i = 0; i < E; ++i) o[i] = sage_i8(x[i], scale, rscale);
+        for (int i = 0; i < E; i += 2) sage_i8x2(x[i], x[i + 1], nscale2, rscale2, o[i], o[i + 1]);
         if (r < rows) store_i8<E>(p.q8 + (bh * S + r0 + r) * D + col, o);
-        // scales exist for the 16-row blocks of Sq padded to 64 rows (all-padding blocks get 1e-7)
-        const int64_t blk16 = (r0 >> 4) + warp;
-        if (lane == 0 && blk16 * 8 < p.nscale) p.qs[bh * p.nscale + blk16 * 8 + g] = scale;
       }
     } else {
       // K: centre as RN_T(k - km), then Sage per-thread groups of 32 rows
@@ -353,6 +397,7 @@ __global__ void __launch_bounds__(kTileThreads, 1) qk_tiles(QKTileParams p) {
       amax = fmaxf(rb[tld], rb[tld + 4]);
       const float scale = __fadd_rn(__fdiv_rn(amax, 127.f), 1e-7f);
       const float rscale = __frcp_rn(scale);
+      const uint64_t nscale2 = pk2f(-scale, -scale), rscale2 = pk2f(rscale, rscale);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int r = 8 * (8 * ih + i) + 2 * tld + hf;
@@ -360,8 +405,7 @@ __global__ void __launch_bounds__(kTileThreads, 1) qk_tiles(QKTileParams p) {
 #pragma unroll
         for (int j = 0; j < E; j += 2) {
           const float2 c = P::unpack(x[i][j / 2]);
-          o[j] = sage_i8(c.x, scale, rscale);
-          o[j + 1] = sage_i8(c.y, scale, rscale);
+          sage_i8x2(c.x, c.y, nscale2, rscale2, o[j], o[j + 1]);
         }
         if (r < rows) store_i8<E>(p.k8 + (bh * S + r0 + r) * D + col, o);
       }
