@@ -478,11 +478,30 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       float lmax = -__int_as_float(0x7f800000);
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
-        float mx = max3f(__uint_as_float(raw[2 * g]), __uint_as_float(raw[2 * g + 1]), __uint_as_float(raw[2 * g + 8]));
-        mx = fmaxf(mx, __uint_as_float(raw[2 * g + 9]));
+        float mx;
+        if constexpr (D == 64) {
+          // two independent chains over K rows 0-7 and 8-15 of the group (a
+          // maximum is exact in any order): half the dependency depth, where
+          // the group's own chain sets the period (config 4: 3.019 vs
+          // 3.047 ms; at D = 128, bound by the score round trip, no gain)
+          float ma = max3f(__uint_as_float(raw[2 * g]), __uint_as_float(raw[2 * g + 1]), __uint_as_float(raw[2 * g + 8]));
+          float mb = max3f(__uint_as_float(raw[64 + 2 * g]), __uint_as_float(raw[64 + 2 * g + 1]),
+                           __uint_as_float(raw[64 + 2 * g + 8]));
+          ma = fmaxf(ma, __uint_as_float(raw[2 * g + 9]));
+          mb = fmaxf(mb, __uint_as_float(raw[64 + 2 * g + 9]));
 #pragma unroll
-        for (int k = 2; k < 16; ++k)
-          mx = max3f(mx, __uint_as_float(raw[8 * k + 2 * g]), __uint_as_float(raw[8 * k + 2 * g + 1]));
+          for (int k = 2; k < 8; ++k) {
+            ma = max3f(ma, __uint_as_float(raw[8 * k + 2 * g]), __uint_as_float(raw[8 * k + 2 * g + 1]));
+            mb = max3f(mb, __uint_as_float(raw[64 + 8 * k + 2 * g]), __uint_as_float(raw[64 + 8 * k + 2 * g + 1]));
+          }
+          mx = fmaxf(ma, mb);
+        } else {
+          mx = max3f(__uint_as_float(raw[2 * g]), __uint_as_float(raw[2 * g + 1]), __uint_as_float(raw[2 * g + 8]));
+          mx = fmaxf(mx, __uint_as_float(raw[2 * g + 9]));
+#pragma unroll
+          for (int k = 2; k < 16; ++k)
+            mx = max3f(mx, __uint_as_float(raw[8 * k + 2 * g]), __uint_as_float(raw[8 * k + 2 * g + 1]));
+        }
         if constexpr (QF8) {
           if (mx > -__int_as_float(0x7f800000)) lmax = fmaxf(lmax, __fmul_rn(mx, f1[g]));
         } else {
