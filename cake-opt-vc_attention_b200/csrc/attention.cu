@@ -622,6 +622,35 @@ int sm_count() {
   return cache[dev];
 }
 
+// One paired-tile CTA per SM.  If the last wave of pairs would be at most half
+// full, the tiles of those pairs (at most one per SM) run on the
+// alternating-tile kernel after the full waves: about 0.6 of a pair period
+// instead of one.  The tail pairs are the last ones of the range, so their
+// units are the range's last ones too.  sms = 0: pairs only.  Host only.
+AttnPlan attention_plan(int64_t qtiles, int64_t ub, int64_t ue, int64_t sms) {
+  AttnPlan r;
+  if (qtiles <= 0 || ub < 0 || ue <= ub) {
+    r.tail_begin = ue;
+    return r;
+  }
+  const int64_t qpairs = (qtiles + 1) / 2;
+  const int64_t pb = (ub / qtiles) * qpairs + (ub % qtiles) / 2;
+  const int64_t pe = ((ue - 1) / qtiles) * qpairs + ((ue - 1) % qtiles) / 2 + 1;
+  const int64_t npairs = pe - pb, tail = sms > 0 ? npairs % sms : 0;
+  r.pairs = npairs;
+  r.tail_begin = ue;
+  r.launches = 1;
+  if (tail > 0 && tail <= sms / 2) {
+    const int64_t first = pe - tail;   // the first tail pair
+    const int64_t ut = (first / qpairs) * qtiles + (first % qpairs) * 2;
+    r.pairs = npairs - tail;
+    r.tail_begin = ut > ub ? ut : ub;
+    r.tail_units = ue - r.tail_begin;
+    r.launches = (r.pairs > 0 ? 1 : 0) + 1;
+  }
+  return r;
+}
+
 int attention_fwd(const AttnArgs& a, cudaStream_t st) {
   const int64_t BH = a.B * a.H;
   const int64_t qtiles = (a.Sq + 127) / 128, ktiles = (a.Sk + 127) / 128;
@@ -663,27 +692,18 @@ int attention_fwd(const AttnArgs& a, cudaStream_t st) {
   // paired-tile kernel: the pairs (two consecutive Q tiles of one head) that meet [ub, ue)
   p.qpairs = (qtiles + 1) / 2;
   const int64_t pb = (ub / qtiles) * p.qpairs + (ub % qtiles) / 2;
-  const int64_t pe = ((ue - 1) / qtiles) * p.qpairs + ((ue - 1) % qtiles) / 2 + 1;
   p.pair_begin = pb;
   p.sm_scale = a.sm_scale;
   p.exact_expcast = a.expcast == 2 ? 1 : 0;
   p.ctl_offset = a.config_control ? 8.0f : 8.807f;
   const int64_t units = ue - ub;
-  // One CTA per SM.  If the last wave of pairs would be at most half full, the
-  // tiles of those pairs (at most one per SM) run on the alternating-tile
-  // kernel after the full waves: about 0.6 of a pair period instead of one.
-  // The tail pairs are the last ones of the range, so their units are the
-  // range's last ones too.
-  const int64_t npairs = pe - pb, sms = sm_count(), tail = npairs % sms;
+  const AttnPlan plan = attention_plan(qtiles, ub, ue, use_pair_only() ? 0 : sm_count());
   Split sp;
-  sp.pairs = npairs;
-  if (!use_pair_only() && tail > 0 && tail <= sms / 2) {
-    const int64_t first = pe - tail;   // the first tail pair
-    const int64_t ut = (first / p.qpairs) * qtiles + (first % p.qpairs) * 2;
-    sp.pairs = npairs - tail;
+  sp.pairs = plan.pairs;
+  if (plan.tail_units > 0) {
     sp.tail = p;
-    sp.tail.unit_begin = ut > ub ? ut : ub;
-    sp.tail_units = ue - sp.tail.unit_begin;
+    sp.tail.unit_begin = plan.tail_begin;
+    sp.tail_units = plan.tail_units;
   }
   if (a.out_dtype == VC_DTYPE_BF16)
     return a.D == 128 ? dispatch_flags<128, __nv_bfloat16>(a, m, p, units, sp, st)

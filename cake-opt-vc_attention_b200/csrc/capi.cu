@@ -469,4 +469,17 @@ int vc_kernel_resources(int head_dim, int64_t* out4) {
   return finish("vc_kernel_resources", attention_resources(head_dim, out4));
 }
 
+int vc_attention_plan(int64_t qtiles, int64_t unit_begin, int64_t unit_end, int sms, int64_t* out4) {
+  if (!out4 || qtiles <= 0 || unit_begin < 0 || unit_end < unit_begin || sms < 0) {
+    set_last_error("vc_attention_plan: needs out4, qtiles > 0, 0 <= unit_begin <= unit_end and sms >= 0");
+    return VC_ERR_ARG;
+  }
+  const AttnPlan r = attention_plan(qtiles, unit_begin, unit_end, sms);
+  out4[0] = r.pairs;
+  out4[1] = r.tail_units;
+  out4[2] = r.tail_begin;
+  out4[3] = r.launches;
+  return VC_OK;
+}
+
 }  // extern "C"

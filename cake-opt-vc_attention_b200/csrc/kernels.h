@@ -99,6 +99,12 @@ struct AttnArgs {
   int config_control; // FP8-P control with the Config contract's scaling (offset 8) instead of Sage's (8.807)
 };
 int attention_fwd(const AttnArgs& a, cudaStream_t st);
+// How attention_fwd spreads units [ub, ue) over its ExpCast kernels (channel
+// V scales): paired-tile CTAs, then tail units on the alternating-tile kernel.
+struct AttnPlan {
+  int64_t pairs = 0, tail_units = 0, tail_begin = 0, launches = 0;
+};
+AttnPlan attention_plan(int64_t qtiles, int64_t ub, int64_t ue, int64_t sms);
 // Copy (and optionally clear) the device error word of each kernel file on the
 // current device.  Synchronous.
 cudaError_t attention_error_word(uint32_t* code, bool clear);

@@ -44,6 +44,7 @@ SIGNATURES = {
     "vc_attention_fwd_e4m3qk": (_i32, [_p, _p, _p, _p, _p, _p, _p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                        _i64, _i32, _i32, _i32, _i64, _f, _i64, _i64, _p]),
     "vc_kernel_resources": (_i32, [_i32, C.POINTER(C.c_int64)]),
+    "vc_attention_plan": (_i32, [C.c_int64, C.c_int64, C.c_int64, _i32, C.POINTER(C.c_int64)]),
     "vc_tensor_peak": (_i32, [_i32, _i32, _i64, _i32, _i32, _i32, _p, _p]),
     "vc_selftest_wait_timeout": (_i32, [_i64, _p, _p]),
 }

@@ -6,6 +6,7 @@ is no CPU path: non-CUDA tensors raise ValueError.
 """
 from __future__ import annotations
 
+import ctypes as C
 import math
 
 import torch
@@ -267,35 +268,21 @@ def attention_fwd(q8, qs, k8, ks, v8, vs, means, *, out_dtype=torch.bfloat16, sm
 
 def attention_plan(qtiles: int, unit_range: tuple[int, int], sms: int) -> dict:
     """How ``attention_fwd`` spreads a unit range over its ExpCast kernels
-    (channel-scaled V, the default kernel choice); the host rule in
-    csrc/attention.cu, restated for launch accounting.
+    (channel-scaled V, the default kernel choice), from the library's own rule
+    (``vc_attention_plan``; host arithmetic, no device needed).
 
-    Units [ub, ue) meet the pairs [pb, pe) (two consecutive Q tiles of one
-    head, ``ceil(qtiles/2)`` pairs per head).  One paired-tile CTA per SM: if
-    the last wave of pairs is at most half full (``0 < npairs % sms <= sms//2``)
-    those pairs' units run on the alternating-tile kernel after the full waves.
+    One paired-tile CTA per SM takes two consecutive Q tiles of a head; if the
+    last wave of pairs is at most half full on ``sms`` SMs, those pairs' units
+    run on the alternating-tile kernel after the full waves.
     Returns ``{"pairs", "tail_units", "tail_begin", "launches"}``.
     """
     ub, ue = unit_range
-    if not 0 <= ub <= ue:
-        raise ValueError("unit_range must satisfy 0 <= begin <= end")
-    if ub == ue:
-        return {"pairs": 0, "tail_units": 0, "tail_begin": ue, "launches": 0}
-    qpairs = (qtiles + 1) // 2
-    pb = (ub // qtiles) * qpairs + (ub % qtiles) // 2
-    pe = ((ue - 1) // qtiles) * qpairs + ((ue - 1) % qtiles) // 2 + 1
-    npairs = pe - pb
-    tail = npairs % sms
-    if tail == 0 or tail > sms // 2:
-        return {"pairs": npairs, "tail_units": 0, "tail_begin": ue, "launches": 1}
-    first = pe - tail
-    ut = max(ub, (first // qpairs) * qtiles + (first % qpairs) * 2)
-    pairs = npairs - tail
-    return {"pairs": pairs, "tail_units": ue - ut, "tail_begin": ut, "launches": (pairs > 0) + 1}
+    out = (C.c_int64 * 4)()
+    N.check(N.load().vc_attention_plan(int(qtiles), int(ub), int(ue), int(sms), out), "vc_attention_plan")
+    return {"pairs": out[0], "tail_units": out[1], "tail_begin": out[2], "launches": out[3]}
 
 
 def kernel_resources(head_dim: int = 128) -> dict:
-    import ctypes as C
     arr = (C.c_int64 * 4)()
     N.check(N.load().vc_kernel_resources(head_dim, arr), "vc_kernel_resources")
     return {"registers_per_thread": arr[0], "static_shared_bytes": arr[1], "dynamic_shared_bytes": arr[2],

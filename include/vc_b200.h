@@ -213,6 +213,16 @@ int vc_selftest_wait_timeout(int64_t budget_ns, int* ok_out, void* stream);
  * Replaces _vc_sm90.kernel_resources (csrc/vc/vc_sm90.cu:788-822). */
 int vc_kernel_resources(int head_dim, int64_t* out4);
 
+/* How vc_attention_fwd spreads the units [unit_begin, unit_end) over its
+ * kernels for ExpCast with channel V scales (host arithmetic only, no device
+ * work): out[0] = paired-tile CTAs (two consecutive 128-row Q tiles of one
+ * head each), out[1] = units that run on the alternating-tile kernel after
+ * them, out[2] = the first of those units, out[3] = attention launches.  The
+ * tail exists when the last wave of pairs is at most half full on ``sms``
+ * streaming multiprocessors (the device's count; 0 = pairs only).
+ * No counterpart in the reference (launch accounting for this library). */
+int vc_attention_plan(int64_t qtiles, int64_t unit_begin, int64_t unit_end, int sms, int64_t* out4);
+
 /* Tensor-core throughput probe, the measured denominator of the attention
  * kernel's roofline (a measurement aid; the reference quotes a nominal peak
  * instead, scripts/profile_int8_h200.py).  Launches ``ctas`` CTAs (one per

@@ -85,6 +85,10 @@ def test_c_abi_rejects_bad_arguments_on_host(lib):
     assert lib.vc_attention_fwd(*args, 1, 0, 1, 0.125, 0, -1, None) == N.VC_ERR_ARG
     assert "block_values" in _last(lib)
     assert lib.vc_kernel_resources(96, None) == N.VC_ERR_ARG
+    out4 = (C.c_int64 * 4)()
+    assert lib.vc_attention_plan(0, 0, 1, 148, out4) == N.VC_ERR_ARG and "qtiles" in _last(lib)
+    assert lib.vc_attention_plan(295, 5, 4, 148, out4) == N.VC_ERR_ARG
+    assert lib.vc_attention_plan(295, 0, 10, 148, None) == N.VC_ERR_ARG
     # failure-detection self-test budget and tensor-peak probe shapes
     assert lib.vc_selftest_wait_timeout(10, None, None) == N.VC_ERR_ARG and "budget_ns" in _last(lib)
     assert lib.vc_tensor_peak(0, 136, 1, 1, 0, 1, None, None) == N.VC_ERR_ARG
